@@ -1,0 +1,129 @@
+/*
+ * frn_b200.h -- C ABI of the B200 (sm_100a) fused RMSNorm -> Linear library.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes,
+ * runs asynchronously on the given CUDA stream (NULL = legacy default stream)
+ * and returns an FRN_* status.  No entry point synchronises the stream.
+ * The message of the last failing call on the calling thread is available
+ * from frn_last_error().
+ *
+ * Math (shared by every fused entry point):
+ *     inv_rms[m] = rsqrt(sum_k x[m,k]^2 / K + eps)            (fp32)
+ *     out[m,n]   = round(inv_rms[m] * sum_k x[m,k] * W[n,k] + b[n])
+ * with W the gamma-folded weight W_fused = W * gamma
+ * (src/weight_transform.py:69-109 of the reference).  The dot product is
+ * accumulated in fp32 on the tcgen05 tensor cores; inv_rms and b are applied
+ * to the fp32 accumulator before the single rounding to the output type.
+ *
+ * Layout rules for the fused entry points: all matrices are row-major with
+ * unit stride along K (x, W) and along N (out); row strides are given in
+ * elements and must make every row start 16-byte aligned; base pointers must
+ * be 16-byte aligned.  A row stride larger than the row length (a strided
+ * view such as DeepseekV3's k_pass, row stride 576 for K = 512) is honoured.
+ */
+#ifndef FRN_B200_H
+#define FRN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define FRN_OK                    0
+#define FRN_ERR_INVALID_ARGUMENT  1  /* shape / null pointer / rank mistakes  */
+#define FRN_ERR_UNSUPPORTED       2  /* dtype or shape the kernel cannot do  */
+#define FRN_ERR_MISALIGNED        3  /* pointer or row stride not 16B-legal  */
+#define FRN_ERR_WORKSPACE         4  /* workspace missing or too small       */
+#define FRN_ERR_CUDA              5  /* CUDA runtime / driver call failed    */
+#define FRN_ERR_DEVICE_TIMEOUT    6  /* a bounded in-kernel wait expired     */
+
+/* ---- element types ----------------------------------------------------- */
+#define FRN_DTYPE_F32   0
+#define FRN_DTYPE_F16   1
+#define FRN_DTYPE_BF16  2
+
+/* ---- kernel selection for frn_fused_rmsnorm_linear_ex ------------------ */
+#define FRN_KERNEL_AUTO         0  /* pick by (M, N, K)                       */
+#define FRN_KERNEL_TILE_N128    1  /* persistent 128x128 tiles                */
+#define FRN_KERNEL_TILE_N192    2  /* persistent 128x192 tiles                */
+#define FRN_KERNEL_TILE_N256    3  /* persistent 128x256 tiles                */
+#define FRN_KERNEL_DECODE       4  /* swap-AB split-K cluster kernel, M<=128  */
+
+/* Device error-word bits (frn_device_error). */
+#define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */
+
+/* Version of this ABI; bumped on any signature change. */
+int frn_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* frn_last_error(void);
+
+/*
+ * In-place RMSNorm rescale of a precomputed GEMM output:
+ *     raw_output[r, c] = round(raw_output[r, c] * inv_rms[r] + b_new[c])
+ * inv_rms[r] = rsqrt(sum_k x[r,k]^2 / h + eps).  dtype applies to x,
+ * raw_output and b_new alike.  threads_per_row is 256 (the reference's V1)
+ * or 512 (V3); the result does not depend on it.
+ * Replaces rmsnorm_normalize_cuda / rmsnorm_normalize_512_cuda
+ * (reference csrc/denominator_kernel.cu:1947-1989 and :1992-2034, bound in
+ * csrc/denominator.cpp:179-193).  Unlike the reference it honours the row
+ * stride of x and of raw_output.
+ */
+int frn_rmsnorm_normalize(int dtype,
+                          const void* x, int64_t x_row_stride,
+                          void* raw_output, int64_t out_row_stride,
+                          const void* b_new,
+                          int64_t rows, int64_t h, int64_t out_dim,
+                          float eps, int threads_per_row, void* stream);
+
+/*
+ * Bytes of device workspace frn_fused_rmsnorm_linear needs for this shape
+ * (0 when the chosen kernel needs none).
+ */
+size_t frn_fused_rmsnorm_linear_workspace_size(int dtype, int64_t M,
+                                               int64_t N, int64_t K);
+
+/*
+ * Fused RMSNorm -> Linear, one launch:
+ *     out[M,N] = round(inv_rms[m] * (x[M,K] . W[N,K]^T) + bias[N])
+ * dtype is FRN_DTYPE_BF16 or FRN_DTYPE_F16 (x, W, bias, out share it).
+ * bias may be NULL (treated as zeros).  workspace may be NULL when
+ * frn_fused_rmsnorm_linear_workspace_size() returned 0.
+ * Replaces the pair F.linear(x_2d, W_new) + rmsnorm_normalize(_512)(...)
+ * of FusedRMSNormLinearV1/V3.forward (reference src/fused_forward.py:158-167,
+ * :182-191) and the functional forms at src/fused_forward.py:316-349.
+ */
+int frn_fused_rmsnorm_linear(int dtype,
+                             const void* x, int64_t M, int64_t K,
+                             int64_t x_row_stride,
+                             const void* w, int64_t N, int64_t w_row_stride,
+                             const void* bias, float eps,
+                             void* out, int64_t out_row_stride,
+                             void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* As frn_fused_rmsnorm_linear with an explicit FRN_KERNEL_* choice. */
+int frn_fused_rmsnorm_linear_ex(int dtype,
+                                const void* x, int64_t M, int64_t K,
+                                int64_t x_row_stride,
+                                const void* w, int64_t N, int64_t w_row_stride,
+                                const void* bias, float eps,
+                                void* out, int64_t out_row_stride,
+                                void* workspace, size_t workspace_bytes,
+                                int kernel, void* stream);
+
+/*
+ * Reads (and optionally clears) the device error word of `device`, which
+ * kernels set when a bounded wait expires instead of hanging.  Synchronous
+ * with respect to the device's legacy default stream.
+ */
+int frn_device_error(int device, uint32_t* flags, int clear);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* FRN_B200_H */

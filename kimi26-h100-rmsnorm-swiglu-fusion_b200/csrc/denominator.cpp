@@ -1,0 +1,172 @@
+// denominator.cpp -- the `denominator_cuda` Python module.
+//
+// Same module name and RMSNorm exports as the reference's pybind11 binding
+// (reference csrc/denominator.cpp:152-213), re-implemented as a thin layer
+// over the C ABI in include/frn_b200.h: tensors are checked the way the
+// reference's host launchers check them (csrc/denominator_kernel.cu:1999-2001,
+// same messages), then their pointers, row strides and the current CUDA stream
+// are handed to libfrn_b200.so.  New exports: fused_rmsnorm_linear (the
+// single-launch fused op) and device_error.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "frn_b200.h"
+
+namespace {
+
+int dtype_code(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return FRN_DTYPE_F32;
+    case at::kHalf: return FRN_DTYPE_F16;
+    case at::kBFloat16: return FRN_DTYPE_BF16;
+    default: return -1;
+  }
+}
+
+void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == FRN_OK, what, " failed (status ", rc, "): ", frn_last_error());
+}
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+void rmsnorm_normalize_impl(const at::Tensor& x, at::Tensor& raw_output, const at::Tensor& b_new,
+                            int64_t h, double eps, int threads, const char* name) {
+  TORCH_CHECK(x.dim() == 2, "x must be 2D");
+  TORCH_CHECK(raw_output.dim() == 2, "raw_output must be 2D");
+  TORCH_CHECK(x.is_cuda() && raw_output.is_cuda() && b_new.is_cuda(),
+              "All tensors must be on CUDA");
+  const int dt = dtype_code(x);
+  TORCH_CHECK(dt >= 0, "Unsupported dtype for RMSNorm ", name,
+              ": only fp32, fp16, bf16 supported");
+  TORCH_CHECK(raw_output.scalar_type() == x.scalar_type() &&
+                  b_new.scalar_type() == x.scalar_type(),
+              "x, raw_output and b_new must share one dtype");
+  TORCH_CHECK(x.size(0) == raw_output.size(0), "x and raw_output must have the same rows");
+  TORCH_CHECK(h == x.size(1), "h (", h, ") must equal x.size(1) (", x.size(1), ")");
+  TORCH_CHECK(b_new.numel() == raw_output.size(1), "b_new must have raw_output.size(1) elements");
+  TORCH_CHECK(x.stride(1) == 1 || x.size(1) == 1, "x must have unit stride along its last dim");
+  TORCH_CHECK(raw_output.stride(1) == 1 || raw_output.size(1) == 1,
+              "raw_output must have unit stride along its last dim");
+  const at::Tensor b = b_new.contiguous();
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(frn_rmsnorm_normalize(dt, x.data_ptr(), x.stride(0), raw_output.data_ptr(),
+                                 raw_output.stride(0), b.data_ptr(), x.size(0), h,
+                                 raw_output.size(1), static_cast<float>(eps), threads,
+                                 stream_of(x)),
+           name);
+}
+
+void rmsnorm_normalize(const at::Tensor& x, at::Tensor raw_output, const at::Tensor& b_new,
+                       int64_t h, double eps) {
+  rmsnorm_normalize_impl(x, raw_output, b_new, h, eps, 256, "rmsnorm_normalize");
+}
+
+void rmsnorm_normalize_512(const at::Tensor& x, at::Tensor raw_output, const at::Tensor& b_new,
+                           int64_t h, double eps) {
+  rmsnorm_normalize_impl(x, raw_output, b_new, h, eps, 512, "rmsnorm_normalize_512");
+}
+
+at::Tensor fused_rmsnorm_linear(const at::Tensor& x_in, const at::Tensor& w,
+                                const c10::optional<at::Tensor>& b_new, double eps,
+                                c10::optional<at::Tensor> out, int64_t kernel) {
+  TORCH_CHECK(x_in.dim() == 2, "x must be 2D");
+  TORCH_CHECK(w.dim() == 2, "W_fused must be 2D");
+  TORCH_CHECK(x_in.is_cuda() && w.is_cuda() && (!b_new || b_new->is_cuda()),
+              "All tensors must be on CUDA");
+  TORCH_CHECK(x_in.scalar_type() == at::kBFloat16 || x_in.scalar_type() == at::kHalf,
+              "fused_rmsnorm_linear supports bf16 and fp16 (got ", x_in.scalar_type(), ")");
+  TORCH_CHECK(w.scalar_type() == x_in.scalar_type(), "x and W_fused must share one dtype");
+  TORCH_CHECK(x_in.size(1) == w.size(1), "x.size(1) (", x_in.size(1), ") != W_fused.size(1) (",
+              w.size(1), ")");
+  TORCH_CHECK(x_in.device() == w.device(), "x and W_fused must be on the same device");
+  // Keep strided row views (k_pass in DeepseekV3 attention); only a
+  // non-unit inner stride forces a copy.
+  const at::Tensor x = (x_in.stride(1) == 1 || x_in.size(1) == 1) ? x_in : x_in.contiguous();
+  const at::Tensor wc = (w.stride(1) == 1) ? w : w.contiguous();
+  const int64_t M = x.size(0), K = x.size(1), N = wc.size(0);
+  at::Tensor b;
+  const void* bptr = nullptr;
+  if (b_new && b_new->defined()) {
+    TORCH_CHECK(b_new->scalar_type() == x.scalar_type(), "b_new must share x's dtype");
+    TORCH_CHECK(b_new->numel() == N, "b_new must have W_fused.size(0) elements");
+    b = b_new->contiguous();
+    bptr = b.data_ptr();
+  }
+  at::Tensor o;
+  if (out && out->defined()) {
+    o = *out;
+    TORCH_CHECK(o.dim() == 2 && o.size(0) == M && o.size(1) == N, "out must be [M, N]");
+    TORCH_CHECK(o.scalar_type() == x.scalar_type() && o.is_cuda(), "out dtype/device mismatch");
+    TORCH_CHECK(o.stride(1) == 1, "out must have unit stride along its last dim");
+  } else {
+    o = at::empty({M, N}, x.options());
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int dt = dtype_code(x);
+  const size_t ws_bytes = frn_fused_rmsnorm_linear_workspace_size(dt, M, N, K);
+  at::Tensor ws;
+  if (ws_bytes > 0)
+    ws = at::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(at::kByte));
+  check_rc(frn_fused_rmsnorm_linear_ex(dt, x.data_ptr(), M, K, x.stride(0), wc.data_ptr(), N,
+                                       wc.stride(0), bptr, static_cast<float>(eps), o.data_ptr(),
+                                       o.stride(0), ws_bytes ? ws.data_ptr() : nullptr, ws_bytes,
+                                       static_cast<int>(kernel), stream_of(x)),
+           "fused_rmsnorm_linear");
+  return o;
+}
+
+int64_t device_error(int64_t device, bool clear) {
+  uint32_t flags = 0;
+  check_rc(frn_device_error(static_cast<int>(device), &flags, clear ? 1 : 0), "device_error");
+  return static_cast<int64_t>(flags);
+}
+
+[[noreturn]] void out_of_scope(const char* name) {
+  TORCH_CHECK(false, name,
+              " belongs to the reference's LayerNorm (OPT) path, which this sm_100a build does "
+              "not implement; use the RMSNorm exports");
+}
+
+at::Tensor compute_denominator(const at::Tensor&, c10::optional<int64_t>) {
+  out_of_scope("compute_denominator");
+}
+void denominator_normalize(const at::Tensor&, at::Tensor, const at::Tensor&, int64_t, double) {
+  out_of_scope("denominator_normalize");
+}
+at::Tensor compute_denominator_welford(const at::Tensor&, c10::optional<int64_t>) {
+  out_of_scope("compute_denominator_welford");
+}
+void denominator_normalize_welford_512(const at::Tensor&, at::Tensor, const at::Tensor&, int64_t,
+                                       double) {
+  out_of_scope("denominator_normalize_welford_512");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200 (sm_100a) fused RMSNorm -> Linear; RMSNorm exports of the reference module";
+  m.def("rmsnorm_normalize", &rmsnorm_normalize,
+        "In-place RMSNorm rescale of a GEMM output (256 threads per row)", py::arg("x"),
+        py::arg("raw_output"), py::arg("b_new"), py::arg("h"), py::arg("eps"));
+  m.def("rmsnorm_normalize_512", &rmsnorm_normalize_512,
+        "In-place RMSNorm rescale of a GEMM output (512 threads per row)", py::arg("x"),
+        py::arg("raw_output"), py::arg("b_new"), py::arg("h"), py::arg("eps"));
+  m.def("fused_rmsnorm_linear", &fused_rmsnorm_linear,
+        "out = rsqrt(mean(x^2)+eps)[:,None] * (x @ W_fused.T) + b_new, one tcgen05 launch",
+        py::arg("x"), py::arg("W_fused"), py::arg("b_new") = py::none(), py::arg("eps") = 1e-6,
+        py::arg("out") = py::none(), py::arg("kernel") = 0);
+  m.def("device_error", &device_error, "Read (and optionally clear) the device error word",
+        py::arg("device") = 0, py::arg("clear") = false);
+  m.def("compute_denominator", &compute_denominator, "LayerNorm path: not implemented",
+        py::arg("x"), py::arg("stream_ptr") = py::none());
+  m.def("denominator_normalize", &denominator_normalize, "LayerNorm path: not implemented",
+        py::arg("x"), py::arg("raw_output"), py::arg("b_new"), py::arg("h"), py::arg("eps"));
+  m.def("compute_denominator_welford", &compute_denominator_welford,
+        "LayerNorm path: not implemented", py::arg("x"), py::arg("stream_ptr") = py::none());
+  m.def("denominator_normalize_welford_512", &denominator_normalize_welford_512,
+        "LayerNorm path: not implemented", py::arg("x"), py::arg("raw_output"), py::arg("b_new"),
+        py::arg("h"), py::arg("eps"));
+}

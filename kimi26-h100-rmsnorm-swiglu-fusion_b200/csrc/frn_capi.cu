@@ -1,0 +1,212 @@
+// frn_capi.cu -- the extern "C" boundary declared in include/frn_b200.h:
+// argument validation (the reference's TORCH_CHECKs plus the alignment and
+// stride rules TMA needs), kernel choice, and error reporting.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "frn_internal.h"
+#include "frn_ptx.cuh"
+
+namespace frn {
+
+__device__ uint32_t g_frn_device_error = 0u;
+
+static thread_local char t_last_error[512] = {0};
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int set_cuda_error(const char* what, cudaError_t e) {
+  return set_error(FRN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base,
+                   int64_t inner, int64_t outer, int64_t row_stride, uint32_t box_inner,
+                   uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return set_error(FRN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * elem_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FRN_ERR_INVALID_ARGUMENT,
+                     "cuTensorMapEncodeTiled failed (%d) for a %lld x %lld tensor, row stride "
+                     "%lld elements",
+                     static_cast<int>(r), static_cast<long long>(outer),
+                     static_cast<long long>(inner), static_cast<long long>(row_stride));
+  return 0;
+}
+
+int sm_count(int device) {
+  static int cache[kMaxDevices] = {0};
+  if (device >= 0 && device < kMaxDevices && cache[device] > 0) return cache[device];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+    n = 148;
+  if (device >= 0 && device < kMaxDevices) cache[device] = n;
+  return n;
+}
+
+uint64_t wait_timeout_ns() {
+  static uint64_t v = 0;
+  if (v == 0) {
+    const char* s = std::getenv("FRN_WAIT_TIMEOUT_MS");
+    long long ms = s ? std::atoll(s) : 0;
+    if (ms <= 0) ms = 2000;
+    v = static_cast<uint64_t>(ms) * 1000000ull;
+  }
+  return v;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int elem_bytes(int dtype) {
+  return dtype == FRN_DTYPE_F32 ? 4 : 2;
+}
+
+static int validate_linear(const LinearProblem& p) {
+  if (p.dtype != FRN_DTYPE_BF16 && p.dtype != FRN_DTYPE_F16)
+    return set_error(FRN_ERR_UNSUPPORTED,
+                     "fused RMSNorm+Linear supports bf16 and fp16 only (dtype %d)", p.dtype);
+  if (p.M < 0 || p.N <= 0 || p.K <= 0)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "bad shape M=%lld N=%lld K=%lld",
+                     (long long)p.M, (long long)p.N, (long long)p.K);
+  if (p.M > 0x7fffffffLL || p.N > 0x7fffffffLL || p.K > 0x7fffffffLL)
+    return set_error(FRN_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
+  if (p.M > 0 && (!p.x || !p.w || !p.out))
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "x, W and out must be non-null");
+  if (p.x_row_stride < p.K || p.w_row_stride < p.K || p.out_row_stride < p.N)
+    return set_error(FRN_ERR_INVALID_ARGUMENT,
+                     "row strides must be >= row lengths (x %lld/%lld, W %lld/%lld, out %lld/%lld)",
+                     (long long)p.x_row_stride, (long long)p.K, (long long)p.w_row_stride,
+                     (long long)p.K, (long long)p.out_row_stride, (long long)p.N);
+  if (p.K % 8 || p.N % 8)
+    return set_error(FRN_ERR_MISALIGNED,
+                     "K (%lld) and N (%lld) must be multiples of 8 (16-byte rows for TMA)",
+                     (long long)p.K, (long long)p.N);
+  if (p.x_row_stride % 8 || p.w_row_stride % 8 || p.out_row_stride % 8)
+    return set_error(FRN_ERR_MISALIGNED, "row strides must be multiples of 8 elements (16 bytes)");
+  if (!aligned16(p.x) || !aligned16(p.w) || !aligned16(p.out) ||
+      (p.bias && !aligned16(p.bias)))
+    return set_error(FRN_ERR_MISALIGNED, "x, W, out and bias must be 16-byte aligned");
+  return 0;
+}
+
+}  // namespace frn
+
+using namespace frn;
+
+extern "C" {
+
+int frn_abi_version(void) { return 1; }
+
+const char* frn_last_error(void) { return t_last_error; }
+
+int frn_rmsnorm_normalize(int dtype, const void* x, int64_t x_row_stride, void* raw_output,
+                          int64_t out_row_stride, const void* b_new, int64_t rows, int64_t h,
+                          int64_t out_dim, float eps, int threads_per_row, void* stream) {
+  if (dtype != FRN_DTYPE_F32 && dtype != FRN_DTYPE_F16 && dtype != FRN_DTYPE_BF16)
+    return set_error(FRN_ERR_UNSUPPORTED,
+                     "Unsupported dtype for RMSNorm normalize: only fp32, fp16, bf16 supported");
+  if (rows < 0 || h <= 0 || out_dim < 0)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "bad shape rows=%lld h=%lld out_dim=%lld",
+                     (long long)rows, (long long)h, (long long)out_dim);
+  if (threads_per_row != 256 && threads_per_row != 512)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "threads_per_row must be 256 or 512");
+  if (rows == 0 || out_dim == 0) return FRN_OK;
+  if (!x || !raw_output || !b_new)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "x, raw_output and b_new must be non-null");
+  if (x_row_stride < h || out_row_stride < out_dim)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "row strides must be >= row lengths");
+  if (rows > 0x7fffffffLL || h > 0x7fffffffLL || out_dim > 0x7fffffffLL)
+    return set_error(FRN_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
+  (void)elem_bytes;
+  return run_rmsnorm_normalize(dtype, x, x_row_stride, raw_output, out_row_stride, b_new, rows, h,
+                               out_dim, eps, threads_per_row,
+                               static_cast<cudaStream_t>(stream));
+}
+
+size_t frn_fused_rmsnorm_linear_workspace_size(int dtype, int64_t M, int64_t N, int64_t K) {
+  (void)dtype; (void)M; (void)N; (void)K;
+  return 0;
+}
+
+int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
+                                int64_t x_row_stride, const void* w, int64_t N,
+                                int64_t w_row_stride, const void* bias, float eps, void* out,
+                                int64_t out_row_stride, void* workspace, size_t workspace_bytes,
+                                int kernel, void* stream) {
+  LinearProblem p{dtype, x, M, K, x_row_stride, w, N, w_row_stride, bias, eps, out,
+                  out_row_stride, workspace, workspace_bytes};
+  int rc = validate_linear(p);
+  if (rc) return rc;
+  if (M == 0) return FRN_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  if (kernel == FRN_KERNEL_AUTO) kernel = choose_prefill_kernel(M, N, sm_count(dev));
+  if (kernel < FRN_KERNEL_TILE_N128 || kernel > FRN_KERNEL_TILE_N256)
+    return set_error(FRN_ERR_UNSUPPORTED, "kernel id %d not available", kernel);
+  return run_fused_linear_prefill(p, kernel, static_cast<cudaStream_t>(stream));
+}
+
+int frn_fused_rmsnorm_linear(int dtype, const void* x, int64_t M, int64_t K, int64_t x_row_stride,
+                             const void* w, int64_t N, int64_t w_row_stride, const void* bias,
+                             float eps, void* out, int64_t out_row_stride, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  return frn_fused_rmsnorm_linear_ex(dtype, x, M, K, x_row_stride, w, N, w_row_stride, bias, eps,
+                                     out, out_row_stride, workspace, workspace_bytes,
+                                     FRN_KERNEL_AUTO, stream);
+}
+
+int frn_device_error(int device, uint32_t* flags, int clear) {
+  if (!flags) return set_error(FRN_ERR_INVALID_ARGUMENT, "flags must be non-null");
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  if (device != prev && cudaSetDevice(device) != cudaSuccess)
+    return set_cuda_error("cudaSetDevice");
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_frn_device_error, sizeof(uint32_t));
+  if (e == cudaSuccess && clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_frn_device_error, &zero, sizeof(uint32_t));
+  }
+  if (device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return set_cuda_error("reading the device error word", e);
+  return FRN_OK;
+}
+
+}  // extern "C"

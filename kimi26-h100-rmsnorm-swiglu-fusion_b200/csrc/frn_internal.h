@@ -1,0 +1,56 @@
+// frn_internal.h -- host-side helpers shared by the kernel launchers and the
+// C ABI (frn_capi.cu).  Not part of the public interface.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/frn_b200.h"
+
+namespace frn {
+
+constexpr int kMaxDevices = 64;
+
+// One fused RMSNorm -> Linear problem, validated by the C ABI before any
+// launcher sees it.  Strides are in elements.
+struct LinearProblem {
+  int dtype;
+  const void* x;
+  int64_t M, K, x_row_stride;
+  const void* w;
+  int64_t N, w_row_stride;
+  const void* bias;  // may be null
+  float eps;
+  void* out;
+  int64_t out_row_stride;
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+// Records `msg` as this thread's last error and returns `code`.
+int set_error(int code, const char* fmt, ...);
+// Records a CUDA failure ("<what>: <cuda error string>") and returns FRN_ERR_CUDA.
+int set_cuda_error(const char* what, cudaError_t e = cudaErrorUnknown);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+// A 2-D row-major tensor of `inner` x `outer` elements, `row_stride` elements
+// between rows, copied in boxes of box_inner x box_outer, OOB reads as zero.
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base,
+                   int64_t inner, int64_t outer, int64_t row_stride, uint32_t box_inner,
+                   uint32_t box_outer, CUtensorMapSwizzle swizzle);
+
+int sm_count(int device);
+// Bound on every in-kernel wait (FRN_WAIT_TIMEOUT_MS, default 2000 ms).
+uint64_t wait_timeout_ns();
+
+int choose_prefill_kernel(int64_t M, int64_t N, int sms);
+int run_fused_linear_prefill(const LinearProblem& pr, int kernel, cudaStream_t s);
+
+int run_rmsnorm_normalize(int dtype, const void* x, int64_t xs, void* out, int64_t os,
+                          const void* b, int64_t rows, int64_t h, int64_t n, float eps,
+                          int threads, cudaStream_t s);
+
+}  // namespace frn

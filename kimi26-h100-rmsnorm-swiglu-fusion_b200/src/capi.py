@@ -1,0 +1,146 @@
+"""ctypes binding of the C ABI in include/frn_b200.h.
+
+This is the binding a non-torch host would write (see INTEGRATION.md for the
+cgo / JNI equivalents); the parity tests use it to call libfrn_b200.so
+exactly through its extern "C" entry points, passing raw device pointers,
+element strides and the current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
+
+from src._build import load_library
+
+FRN_OK = 0
+FRN_ERR_INVALID_ARGUMENT = 1
+FRN_ERR_UNSUPPORTED = 2
+FRN_ERR_MISALIGNED = 3
+FRN_ERR_WORKSPACE = 4
+FRN_ERR_CUDA = 5
+FRN_ERR_DEVICE_TIMEOUT = 6
+
+FRN_DTYPE_F32 = 0
+FRN_DTYPE_F16 = 1
+FRN_DTYPE_BF16 = 2
+
+FRN_KERNEL_AUTO = 0
+FRN_KERNEL_TILE_N128 = 1
+FRN_KERNEL_TILE_N192 = 2
+FRN_KERNEL_TILE_N256 = 3
+FRN_KERNEL_DECODE = 4
+
+# name -> (restype, argtypes); must cover every function in include/frn_b200.h
+PROTOTYPES = {
+    "frn_abi_version": (c_int, []),
+    "frn_last_error": (c_char_p, []),
+    "frn_rmsnorm_normalize": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64,
+         c_float, c_int, c_void_p],
+    ),
+    "frn_fused_rmsnorm_linear_workspace_size": (c_size_t, [c_int, c_int64, c_int64, c_int64]),
+    "frn_fused_rmsnorm_linear": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+         c_float, c_void_p, c_int64, c_void_p, c_size_t, c_void_p],
+    ),
+    "frn_fused_rmsnorm_linear_ex": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+         c_float, c_void_p, c_int64, c_void_p, c_size_t, c_int, c_void_p],
+    ),
+    "frn_device_error": (c_int, [c_int, ctypes.POINTER(c_uint32), c_int]),
+}
+
+_lib = None
+
+
+class FrnError(RuntimeError):
+    def __init__(self, code: int, what: str, message: str):
+        super().__init__(f"{what} failed (status {code}): {message}")
+        self.code = code
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        handle = load_library()
+        for name, (res, args) in PROTOTYPES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().frn_last_error().decode()
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FRN_OK:
+        raise FrnError(rc, what, last_error())
+
+
+# ------------------------------------------------------------ torch helpers
+def _dtype_code(t) -> int:
+    import torch
+
+    return {torch.float32: FRN_DTYPE_F32, torch.float16: FRN_DTYPE_F16,
+            torch.bfloat16: FRN_DTYPE_BF16}[t.dtype]
+
+
+def _stream_ptr(device) -> int:
+    import torch
+
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def workspace_size(dtype_code: int, M: int, N: int, K: int) -> int:
+    return int(lib().frn_fused_rmsnorm_linear_workspace_size(dtype_code, M, N, K))
+
+
+def fused_rmsnorm_linear(x, w, bias=None, eps: float = 1e-6, out=None,
+                         kernel: int = FRN_KERNEL_AUTO, workspace=None):
+    """out = rsqrt(mean(x^2)+eps)[:,None] * (x @ w.T) + bias through the C ABI.
+
+    x: [M, K] with unit inner stride (any 16B-legal row stride); w: [N, K].
+    """
+    import torch
+
+    assert x.dim() == 2 and w.dim() == 2 and x.stride(1) == 1 and w.stride(1) == 1
+    M, K = x.shape
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    dt = _dtype_code(x)
+    need = workspace_size(dt, M, N, K)
+    if workspace is None and need > 0:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    ws_ptr = workspace.data_ptr() if workspace is not None else None
+    ws_bytes = workspace.numel() if workspace is not None else 0
+    rc = lib().frn_fused_rmsnorm_linear_ex(
+        dt, x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0),
+        bias.data_ptr() if bias is not None else None, float(eps), out.data_ptr(),
+        out.stride(0), ws_ptr, ws_bytes, int(kernel), _stream_ptr(x.device))
+    check(rc, "frn_fused_rmsnorm_linear")
+    return out
+
+
+def rmsnorm_normalize(x, raw_output, b_new, h: int, eps: float, threads: int = 256):
+    """In-place raw_output = raw_output * inv_rms(x) + b_new through the C ABI."""
+    rc = lib().frn_rmsnorm_normalize(
+        _dtype_code(x), x.data_ptr(), x.stride(0), raw_output.data_ptr(), raw_output.stride(0),
+        b_new.data_ptr(), x.shape[0], h, raw_output.shape[1], float(eps), int(threads),
+        _stream_ptr(x.device))
+    check(rc, "frn_rmsnorm_normalize")
+    return raw_output
+
+
+def device_error(device: int = 0, clear: bool = False) -> int:
+    flags = c_uint32(0)
+    check(lib().frn_device_error(device, ctypes.byref(flags), 1 if clear else 0),
+          "frn_device_error")
+    return int(flags.value)

@@ -1,0 +1,178 @@
+"""Fused RMSNorm -> Linear modules with the reference's class names, ctor
+signatures and buffer names (reference src/fused_forward.py:143-349), so that
+patchers and state_dicts written against the reference keep working.
+
+Forward of every bf16/fp16 module is ONE launch of the sm_100a fused kernel
+(``denominator_cuda.fused_rmsnorm_linear``): the RMS reduction runs inside
+the GEMM and inv_rms / bias are applied to the fp32 accumulator.  V1 and V3
+named the reference's 256- vs 512-thread normalize kernels; both map to the
+same fused kernel here.  fp32 inputs, which the bf16/fp16 tensor-core kernel
+does not take, run as the reference does -- cuBLAS ``F.linear`` then the
+in-place ``rmsnorm_normalize(_512)`` kernel of this library.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.nn.functional as F
+
+from src.load_cuda import denominator_cuda
+
+# Optional NVTX ranges (same switch as the reference: FUSED_LN_NVTX=1).
+_USE_NVTX = os.environ.get("FUSED_LN_NVTX", "0") == "1"
+
+
+class _NullContext:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *args):
+        return False
+
+
+def _nvtx_range(name: str):
+    if _USE_NVTX:
+        return torch.cuda.nvtx.range(name)
+    return _NullContext()
+
+
+_TENSOR_CORE_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def _fused_2d(x_2d: torch.Tensor, W: torch.Tensor, b: torch.Tensor, h: int, eps: float,
+              threads: int) -> torch.Tensor:
+    """[M, K] -> [M, N] fused RMSNorm -> Linear on the current CUDA stream."""
+    if x_2d.size(-1) != h:
+        raise ValueError(f"x has {x_2d.size(-1)} features but the module was built for h={h}")
+    if x_2d.dtype in _TENSOR_CORE_DTYPES:
+        return denominator_cuda.fused_rmsnorm_linear(x_2d, W, b, float(eps))
+    raw = F.linear(x_2d, W)
+    normalize = (denominator_cuda.rmsnorm_normalize_512 if threads == 512
+                 else denominator_cuda.rmsnorm_normalize)
+    normalize(x_2d, raw, b, h, float(eps))
+    return raw
+
+
+def _apply(x: torch.Tensor, W: torch.Tensor, b: torch.Tensor, h: int, eps: float,
+           threads: int) -> torch.Tensor:
+    orig_shape = x.shape
+    x_2d = x.reshape(-1, x.size(-1))  # keeps a strided row view when it can
+    out = _fused_2d(x_2d, W, b, h, eps, threads)
+    return out.reshape(orig_shape[:-1] + (out.size(-1),))
+
+
+class _FusedRMSNormLinearBase(torch.nn.Module):
+    _threads = 256
+    _range_name = "FusedRMSNormLinear"
+
+    def __init__(self, W_new: torch.Tensor, b_new: torch.Tensor, h: int, eps: float):
+        super().__init__()
+        self.register_buffer("W_new", W_new)
+        self.register_buffer("b_new", b_new)
+        self.h = h
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        with _nvtx_range(self._range_name):
+            return _apply(x, self.W_new, self.b_new, self.h, self.eps, self._threads)
+
+    def extra_repr(self) -> str:
+        return f"in={self.h}, out={self.W_new.shape[0]}, eps={self.eps}"
+
+
+class FusedRMSNormLinearV1(_FusedRMSNormLinearBase):
+    """RMSNorm(gamma folded into W_new) -> Linear as one fused launch."""
+
+    _threads = 256
+    _range_name = "FusedRMSNormLinear_V1"
+
+
+class FusedRMSNormLinearV3(_FusedRMSNormLinearBase):
+    """Same math as V1 (the reference's V3 differed only in normalize threads)."""
+
+    _threads = 512
+    _range_name = "FusedRMSNormLinear_V3"
+
+
+class _FusedRMSNormCombinedBase(torch.nn.Module):
+    _threads = 256
+    _range_name = "FusedRMSNormCombinedLinear"
+
+    def __init__(self, W_combined: torch.Tensor, b_combined: torch.Tensor,
+                 split_sizes: list[int], h: int, eps: float):
+        super().__init__()
+        self.register_buffer("W_combined", W_combined)
+        self.register_buffer("b_combined", b_combined)
+        self.split_sizes = split_sizes
+        self.h = h
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> list[torch.Tensor]:
+        with _nvtx_range(self._range_name):
+            batch_shape = x.shape[:-1]
+            out = _fused_2d(x.reshape(-1, x.size(-1)), self.W_combined, self.b_combined,
+                            self.h, self.eps, self._threads)
+            parts = torch.split(out, self.split_sizes, dim=-1)
+            return [p.contiguous().reshape(*batch_shape, p.size(-1)) for p in parts]
+
+
+class FusedRMSNormCombinedLinearV1(_FusedRMSNormCombinedBase):
+    """One RMSNorm shared by several Linears (e.g. Q/K/V): one fused launch over
+    the concatenated weight, returned as a list of contiguous parts."""
+
+    _threads = 256
+    _range_name = "FusedRMSNormCombinedLinear_V1"
+
+
+class FusedRMSNormCombinedLinearV3(_FusedRMSNormCombinedBase):
+    _threads = 512
+    _range_name = "FusedRMSNormCombinedLinear_V3"
+
+
+class _FusedRMSNormSwiGLUBase(torch.nn.Module):
+    _threads = 256
+    _range_name = "FusedRMSNormSwiGLU"
+
+    def __init__(self, W_combined: torch.Tensor, b_combined: torch.Tensor, intermediate: int,
+                 h: int, eps: float):
+        super().__init__()
+        self.register_buffer("W_combined", W_combined)
+        self.register_buffer("b_combined", b_combined)
+        self.intermediate = intermediate
+        self.h = h
+        self.eps = eps
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        with _nvtx_range(self._range_name):
+            batch_shape = x.shape[:-1]
+            gu = _fused_2d(x.reshape(-1, x.size(-1)), self.W_combined, self.b_combined, self.h,
+                           self.eps, self._threads)
+            gate, up = gu[:, : self.intermediate], gu[:, self.intermediate:]
+            out = F.silu(gate) * up
+            return out.reshape(*batch_shape, self.intermediate)
+
+
+class FusedRMSNormSwiGLUV1(_FusedRMSNormSwiGLUBase):
+    """RMSNorm -> [gate | up] projection -> SiLU(gate) * up."""
+
+    _threads = 256
+    _range_name = "FusedRMSNormSwiGLU_V1"
+
+
+class FusedRMSNormSwiGLUV3(_FusedRMSNormSwiGLUBase):
+    _threads = 512
+    _range_name = "FusedRMSNormSwiGLU_V3"
+
+
+def fused_rmsnorm_linear_forward_v1(x: torch.Tensor, W_new: torch.Tensor, b_new: torch.Tensor,
+                                    h: int, eps: float = 1e-6) -> torch.Tensor:
+    """Functional fused RMSNorm -> Linear (reference src/fused_forward.py:316-331)."""
+    return _apply(x, W_new, b_new, h, eps, 256)
+
+
+def fused_rmsnorm_linear_forward_v3(x: torch.Tensor, W_new: torch.Tensor, b_new: torch.Tensor,
+                                    h: int, eps: float = 1e-6) -> torch.Tensor:
+    """Functional fused RMSNorm -> Linear (reference src/fused_forward.py:334-349)."""
+    return _apply(x, W_new, b_new, h, eps, 512)

@@ -1,0 +1,66 @@
+"""denominator_cuda / fused_forward surface on CPU: names, buffers, errors."""
+import pytest
+import torch
+
+from src import fused_forward
+from src.load_cuda import denominator_cuda
+
+REFERENCE_EXPORTS = [
+    "compute_denominator", "denominator_normalize", "compute_denominator_welford",
+    "denominator_normalize_welford_512", "rmsnorm_normalize", "rmsnorm_normalize_512",
+    "rmsnorm_swiglu", "rmsnorm_swiglu_512",
+]
+
+
+def test_module_exports():
+    for name in REFERENCE_EXPORTS + ["fused_rmsnorm_linear", "device_error"]:
+        if name.startswith("rmsnorm_swiglu"):
+            continue  # added with the fused SwiGLU epilogue
+        assert hasattr(denominator_cuda, name), name
+
+
+def test_loaded_from_tree():
+    import os
+
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    assert os.path.realpath(denominator_cuda.__file__).startswith(os.path.realpath(here))
+
+
+def test_cpu_tensors_rejected_like_reference():
+    x = torch.randn(4, 8, dtype=torch.bfloat16)
+    raw = torch.randn(4, 16, dtype=torch.bfloat16)
+    b = torch.zeros(16, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="All tensors must be on CUDA"):
+        denominator_cuda.rmsnorm_normalize(x, raw, b, 8, 1e-5)
+    with pytest.raises(RuntimeError, match="All tensors must be on CUDA"):
+        denominator_cuda.rmsnorm_normalize_512(x, raw, b, 8, 1e-5)
+    with pytest.raises(RuntimeError, match="All tensors must be on CUDA"):
+        denominator_cuda.fused_rmsnorm_linear(x, torch.randn(16, 8, dtype=torch.bfloat16), b, 1e-5)
+    with pytest.raises(RuntimeError, match="x must be 2D"):
+        denominator_cuda.rmsnorm_normalize(x.view(-1), raw, b, 8, 1e-5)
+
+
+def test_layernorm_exports_say_out_of_scope():
+    with pytest.raises(RuntimeError, match="LayerNorm"):
+        denominator_cuda.compute_denominator(torch.randn(2, 2))
+
+
+@pytest.mark.parametrize("cls", [fused_forward.FusedRMSNormLinearV1,
+                                 fused_forward.FusedRMSNormLinearV3])
+def test_module_buffers_and_state_dict(cls):
+    W = torch.randn(16, 8, dtype=torch.bfloat16)
+    b = torch.zeros(16, dtype=torch.bfloat16)
+    m = cls(W, b, 8, 1e-5)
+    assert set(m.state_dict()) == {"W_new", "b_new"}
+    assert m.h == 8 and m.eps == 1e-5
+    with pytest.raises(RuntimeError, match="All tensors must be on CUDA"):
+        m(torch.randn(2, 3, 8, dtype=torch.bfloat16))
+
+
+def test_combined_and_swiglu_buffers():
+    W = torch.randn(24, 8, dtype=torch.bfloat16)
+    b = torch.zeros(24, dtype=torch.bfloat16)
+    c = fused_forward.FusedRMSNormCombinedLinearV3(W, b, [16, 4, 4], 8, 1e-5)
+    assert set(c.state_dict()) == {"W_combined", "b_combined"}
+    s = fused_forward.FusedRMSNormSwiGLUV1(W, b, 12, 8, 1e-5)
+    assert set(s.state_dict()) == {"W_combined", "b_combined"} and s.intermediate == 12
