@@ -47,10 +47,15 @@ extern "C" {
 
 /* ---- kernel selection for frn_fused_rmsnorm_linear_ex ------------------ */
 #define FRN_KERNEL_AUTO         0  /* pick by (M, N, K)                       */
-#define FRN_KERNEL_TILE_N128    1  /* persistent 128x128 tiles                */
-#define FRN_KERNEL_TILE_N192    2  /* persistent 128x192 tiles                */
-#define FRN_KERNEL_TILE_N256    3  /* persistent 128x256 tiles                */
+#define FRN_KERNEL_TILE_N128    1  /* one SM per 128x128 tile                 */
+#define FRN_KERNEL_TILE_N192    2  /* one SM per 128x192 tile                 */
+#define FRN_KERNEL_TILE_N256    3  /* one SM per 128x256 tile                 */
 #define FRN_KERNEL_DECODE       4  /* swap-AB split-K cluster kernel, M<=128  */
+#define FRN_KERNEL_PAIR_N128    5  /* SM pair (cta_group::2) per 256x128 tile */
+#define FRN_KERNEL_PAIR_N160    6  /* SM pair per 256x160 tile                */
+#define FRN_KERNEL_PAIR_N192    7  /* SM pair per 256x192 tile                */
+#define FRN_KERNEL_PAIR_N224    8  /* SM pair per 256x224 tile                */
+#define FRN_KERNEL_PAIR_N256    9  /* SM pair per 256x256 tile                */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */

@@ -178,10 +178,16 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
   if (M == 0) return FRN_OK;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
-  if (kernel == FRN_KERNEL_AUTO) kernel = choose_prefill_kernel(M, N, sm_count(dev));
-  if (kernel < FRN_KERNEL_TILE_N128 || kernel > FRN_KERNEL_TILE_N256)
-    return set_error(FRN_ERR_UNSUPPORTED, "kernel id %d not available", kernel);
-  return run_fused_linear_prefill(p, kernel, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kernel == FRN_KERNEL_AUTO)
+    return run_fused_linear_pair(p, choose_pair_kernel(M, N, sm_count(dev) / 2), s);
+  if (kernel >= FRN_KERNEL_TILE_N128 && kernel <= FRN_KERNEL_TILE_N256)
+    return run_fused_linear_prefill(p, kernel, s);
+  if (kernel >= FRN_KERNEL_PAIR_N128 && kernel <= FRN_KERNEL_PAIR_N256) {
+    static const int bns[5] = {128, 160, 192, 224, 256};
+    return run_fused_linear_pair(p, bns[kernel - FRN_KERNEL_PAIR_N128], s);
+  }
+  return set_error(FRN_ERR_UNSUPPORTED, "kernel id %d not available", kernel);
 }
 
 int frn_fused_rmsnorm_linear(int dtype, const void* x, int64_t M, int64_t K, int64_t x_row_stride,

@@ -1,0 +1,449 @@
+// frn_fused_linear_pair.cu -- fused RMSNorm -> Linear on SM pairs (cta_group::2).
+//
+// Same math as frn_fused_linear.cu; one 256 x BN output tile per CTA pair:
+// tcgen05.mma.cta_group::2 with M = 256 reads A (x rows) from both CTAs'
+// shared memory (128 rows each) and B (W rows) split in two halves of BN/2
+// rows, so every SM loads 16 KB of x and BN*64 B of W per 64-deep k-block
+// instead of 16 KB + BN*128 B: the L2 -> SM traffic per MMA halves for W.
+//
+// Roles (each CTA of the pair):
+//   warps 0-3   epilogue: TMEM lanes of this CTA's 128 rows -> acc * inv_rms
+//               + b -> one rounding -> swizzled smem block per warp -> full
+//               128-byte row segments stored to global (coalesced).
+//   warps 4-7   TMA producers: x tile / W half-tile, each split over even and
+//               odd stages (four issuing threads, because one thread keeps
+//               only a few bulk-tensor loads in flight).  Both CTAs' loads
+//               complete on the EVEN CTA's `full` barrier, which the even
+//               CTA's x-producers arm with the bytes of the whole pair.
+//   warp 8      even CTA: single-thread MMA issuer; every CTA: TMEM owner.
+//               After each k-block the MMA commit is multicast to both CTAs'
+//               `mma_done[stage]`; after each tile to both `tmem_full[acc]`.
+//   warps 9-12  RMS reducers: once the MMA has consumed a stage, thread t
+//               sums x[row t]^2 from this CTA's copy of the stage and then
+//               frees the stage (empty barrier, 4 arrivals).  Only the first
+//               tile of each run of same-m-block tiles is reduced; later
+//               tiles reuse the cached inv_rms and just free the stages.
+// The epilogue warps of both CTAs release an accumulator by arriving on the
+// even CTA's `tmem_empty[acc]` (8 arrivals).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "frn_internal.h"
+#include "frn_ptx.cuh"
+
+namespace frn {
+
+struct PairParams {
+  int32_t M, N, K;
+  int32_t num_m_blocks;  // of 256 rows
+  int32_t num_n_blocks;  // of BN columns
+  int32_t num_k_blocks;  // of 64
+  float eps;
+  const void* bias;  // may be null
+  void* out;
+  int64_t out_row_stride;  // elements
+  uint64_t timeout_ns;
+};
+
+template <int BN, int STAGES>
+struct PairCfg {
+  static constexpr int BM = 128;  // rows per CTA
+  static constexpr int BK = 64;
+  static constexpr int BN_HALF = BN / 2;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN_HALF * BK * 2;
+  static constexpr uint32_t PAIR_TX = 2u * (A_BYTES + B_BYTES);
+  static constexpr uint32_t TMEM_COLS = (2 * BN <= 256) ? 256u : 512u;
+  static constexpr int STG_BYTES = 32 * 128;  // one warp's 32 rows x 64 columns
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_STG = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_RMS = OFF_STG + 4 * 2 * STG_BYTES;
+  static constexpr int OFF_BAR = OFF_RMS + 2 * BM * 4;
+  static constexpr int NUM_BARS = 3 * STAGES + 9;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int RMS_WARPS = 4;
+  static constexpr int WARP_PROD0 = 4;  // warps 4..7: (x | W) x (even | odd stages)
+  static constexpr int WARP_MMA = 8;
+  static constexpr int WARP_RMS0 = 9;
+  static constexpr int THREADS = 32 * (EPI_WARPS + 5 + RMS_WARPS);
+  static_assert(STAGES % 2 == 0, "stages are split between two producers per operand");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(B_BYTES % 1024 == 0, "stage buffers must stay 1024-aligned");
+  static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
+};
+
+template <typename T, int BN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>::THREADS, 1)
+    fused_rmsnorm_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                     const __grid_constant__ CUtensorMap tmap_w,
+                                     const PairParams p) {
+  using C = PairCfg<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);  // used in the even CTA
+  uint64_t* mma_done = full + STAGES;
+  uint64_t* empty = mma_done + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;  // used in the even CTA
+  uint64_t* rms_full = tmem_empty + 2;
+  uint64_t* rms_empty = rms_full + 2;
+  uint64_t* drain = rms_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* rms_buf = reinterpret_cast<float*>(smem + C::OFF_RMS);
+
+  const uint32_t warp = warp_id_in_cta();
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t rank = cluster_cta_rank();  // 0 = even CTA (MMA issuer), 1 = odd
+  const uint32_t pair = blockIdx.x >> 1;
+  const uint32_t num_pairs = gridDim.x >> 1;
+
+  if (warp == C::WARP_PROD0 && lane == 0) {
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&mma_done[s], 1);
+      mbar_init(&empty[s], C::RMS_WARPS);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 2 * C::EPI_WARPS);
+      mbar_init(&rms_full[a], C::RMS_WARPS);
+      mbar_init(&rms_empty[a], C::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_mbarrier_init();
+  }
+  if (warp == C::WARP_MMA) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  // Both CTAs' barriers must be initialised before either signals the other.
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  const int nkb = p.num_k_blocks;
+  const uint64_t to = p.timeout_ns;
+
+  if (warp >= C::WARP_PROD0 && warp < C::WARP_PROD0 + 4) {
+    // Four issuing threads: a single thread keeps only a few bulk-tensor loads
+    // in flight, so x and W loads are split by operand and by stage parity.
+    if (lane == 0) {
+      griddep_wait();
+      const uint32_t pid = warp - C::WARP_PROD0;
+      const bool is_a = (pid & 1u) == 0;
+      const uint32_t parity_sel = pid >> 1;  // this thread fills stages with s % 2 == parity_sel
+      const bool arms = is_a && rank == 0;
+      uint32_t stage = 0, phase = 0;
+      for (int t = pair; t < num_tiles; t += num_pairs) {
+        const int m0 = (t % p.num_m_blocks) * 2 * C::BM + rank * C::BM;
+        const int n0 = (t / p.num_m_blocks) * BN + rank * C::BN_HALF;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if ((stage & 1u) == parity_sel) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, to)) { ok = false; break; }
+            const uint32_t leader_full = mapa_shared(smem_addr(&full[stage]), 0);
+            if (arms) mbar_arrive_expect_tx(&full[stage], C::PAIR_TX);
+            if (is_a)
+              tma_load_2d_pair(smem + C::OFF_A + stage * C::A_BYTES, &tmap_x, leader_full,
+                               kb * C::BK, m0);
+            else
+              tma_load_2d_pair(smem + C::OFF_B + stage * C::B_BYTES, &tmap_w, leader_full,
+                               kb * C::BK, n0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == C::WARP_MMA) {
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = make_idesc_f16(Elem16<T>::kUmmaFormat, 2 * C::BM, BN);
+      uint32_t stage = 0, phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+        const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(smem + C::OFF_A + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / 16; ++k) {
+            umma_f16_ss_pair(d_tmem, make_smem_desc_k_sw128(a_addr + k * 32),
+                             make_smem_desc_k_sw128(b_addr + k * 32), idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair_mc(&mma_done[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&tmem_full[acc], 0x3);
+      }
+      umma_commit_pair_mc(drain, 0x1);
+      uint32_t zero = 0;
+      mbar_wait(drain, 0, &zero, to);
+    }
+  } else if (warp >= C::WARP_RMS0) {
+    // inv_rms depends only on the m-block, so it is reduced on the first tile
+    // of each run of consecutive tiles with the same m-block (a "generation")
+    // and kept in rms_buf[gen & 1] until the epilogue has finished the run.
+    const int r = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;  // row in this CTA's half
+    const float inv_k = 1.0f / static_cast<float>(p.K);
+    uint32_t stage = 0, phase = 0;
+    int gen = -1, cur_m = -1;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+      const int mb = t % p.num_m_blocks;
+      const bool first = (mb != cur_m);
+      if (first) { ++gen; cur_m = mb; }
+      float ss0 = 0.f, ss1 = 0.f;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
+        const uint8_t* row = smem + C::OFF_A + stage * C::A_BYTES + r * 128;
+        if (first)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (r & 7)) << 4));
+          const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
+          const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
+          ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
+          ss0 = fmaf(f1.x, f1.x, ss0); ss1 = fmaf(f1.y, f1.y, ss1);
+          ss0 = fmaf(f2.x, f2.x, ss0); ss1 = fmaf(f2.y, f2.y, ss1);
+          ss0 = fmaf(f3.x, f3.x, ss0); ss1 = fmaf(f3.y, f3.y, ss1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok || !first) continue;
+      const uint32_t g = static_cast<uint32_t>(gen);
+      if (!mbar_wait(&rms_empty[g & 1], ((g >> 1) & 1) ^ 1u, abort_flag, to)) break;
+      rms_buf[(g & 1) * C::BM + r] = rsqrtf((ss0 + ss1) * inv_k + p.eps);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rms_full[g & 1]);
+    }
+  } else {
+    // Epilogue: warp q owns TMEM lanes [32q, 32q+32) = rows of this CTA's half.
+    const uint32_t q = warp;
+    const bool has_bias = p.bias != nullptr;
+    const uint4* bias16 = reinterpret_cast<const uint4*>(p.bias);
+    const uint32_t leader_tmem_empty0 = mapa_shared(smem_addr(&tmem_empty[0]), 0);
+    griddep_wait();
+    int i = 0;
+    int gen = -1, cur_m = -1;
+    float inv_rms = 0.f;
+    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
+      const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+      const int mb = t % p.num_m_blocks;
+      const int row = mb * 2 * C::BM + rank * C::BM + q * 32 + lane;
+      const int n0 = (t / p.num_m_blocks) * BN;
+      const bool first = (mb != cur_m);
+      const bool last = (t + static_cast<int>(num_pairs) >= num_tiles) ||
+                        ((t + static_cast<int>(num_pairs)) % p.num_m_blocks != mb);
+      if (first) { ++gen; cur_m = mb; }
+      const uint32_t g = static_cast<uint32_t>(gen);
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) break;
+      if (first) {
+        if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) break;
+        inv_rms = rms_buf[(g & 1) * C::BM + q * 32 + lane];
+      }
+      tc_fence_after();
+      if (last) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
+      }
+      const int row_base = row - static_cast<int>(lane);  // first row of this warp
+      const uint32_t taddr = tmem_base + acc * BN + ((q * 32u) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN / 64 + (BN % 64 ? 1 : 0); ++c) {
+        // 64 columns (the last chunk may be 32): TMEM -> fp32 -> scale/bias ->
+        // bf16 into a 128B-swizzled [32 rows x 128 B] smem block, then each
+        // quarter-warp writes one full 128-byte row segment to global.
+        const bool half = (c * 64 + 32 >= BN);
+        uint32_t v[64];
+        tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_wait();
+        if (c == BN / 64 + (BN % 64 ? 1 : 0) - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
+        }
+        uint8_t* sb = smem + C::OFF_STG + (q * 2 + (c & 1)) * C::STG_BYTES;
+        const int col0 = n0 + c * 64;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // 16-byte chunk j = columns [8j, 8j+8)
+          if (half && j >= 4) break;
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) * inv_rms;
+          const int col = col0 + j * 8;
+          if (has_bias && col < p.N) {
+            const uint4 bv = __ldg(bias16 + col / 8);
+            const float2 b0 = pair_to_float2<T>(bv.x), b1 = pair_to_float2<T>(bv.y);
+            const float2 b2 = pair_to_float2<T>(bv.z), b3 = pair_to_float2<T>(bv.w);
+            f[0] += b0.x; f[1] += b0.y; f[2] += b1.x; f[3] += b1.y;
+            f[4] += b2.x; f[5] += b2.y; f[6] += b3.x; f[7] += b3.y;
+          }
+          uint4 o;
+          o.x = float2_to_pair<T>(f[0], f[1]);
+          o.y = float2_to_pair<T>(f[2], f[3]);
+          o.z = float2_to_pair<T>(f[4], f[5]);
+          o.w = float2_to_pair<T>(f[6], f[7]);
+          *reinterpret_cast<uint4*>(sb + lane * 128 + ((j ^ (lane & 7)) << 4)) = o;
+        }
+        __syncwarp();
+        // Read back: thread -> (row r = i*4 + lane/8, 16-byte chunk lane%8).
+        const int chunk = static_cast<int>(lane & 7);
+        const int col = col0 + chunk * 8;
+        const bool col_ok = col < p.N && !(half && chunk >= 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = i * 4 + static_cast<int>(lane >> 3);
+          const uint4 o = *reinterpret_cast<const uint4*>(sb + r * 128 + ((chunk ^ (r & 7)) << 4));
+          const int grow = row_base + r;
+          if (col_ok && grow < p.M)
+            st_global_v4(static_cast<T*>(p.out) + static_cast<int64_t>(grow) * p.out_row_stride + col,
+                         o.x, o.y, o.z, o.w);
+        }
+      }
+    }
+  }
+
+  // Every thread of both CTAs gets here (all waits are bounded), so the pair
+  // never leaves with the other CTA still reading its smem or barriers.
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+  if (*abort_flag) {
+    // A wait expired: give in-flight bulk copies into this CTA time to land.
+    __nanosleep(20000);
+  }
+  if (warp == C::WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <typename T, int BN, int STAGES>
+static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
+  using C = PairCfg<BN, STAGES>;
+  auto kern = fused_rmsnorm_linear_pair_kernel<T, BN, STAGES>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  static int max_pairs[kMaxDevices] = {};
+  if (dev < kMaxDevices && max_pairs[dev] == 0) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(pair kernel)", e);
+    cudaLaunchConfig_t qc = {};
+    qc.gridDim = dim3(2 * 74);
+    qc.blockDim = dim3(C::THREADS);
+    qc.dynamicSmemBytes = C::SMEM_BYTES;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    qc.attrs = qa;
+    qc.numAttrs = 1;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &qc);
+    if (e != cudaSuccess || clusters <= 0) clusters = sm_count(dev) / 2;
+    max_pairs[dev] = clusters;
+  }
+  const int pairs_avail = dev < kMaxDevices ? max_pairs[dev] : sm_count(dev) / 2;
+
+  const CUtensorMapDataType dt = Elem16<T>::kTmaType;
+  CUtensorMap tx, tw;
+  int rc = encode_tmap_2d(&tx, dt, 2, pr.x, pr.K, pr.M, pr.x_row_stride, C::BK, C::BM,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tw, dt, 2, pr.w, pr.K, pr.N, pr.w_row_stride, C::BK, C::BN_HALF,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+
+  PairParams p;
+  p.M = static_cast<int32_t>(pr.M);
+  p.N = static_cast<int32_t>(pr.N);
+  p.K = static_cast<int32_t>(pr.K);
+  p.num_m_blocks = static_cast<int32_t>((pr.M + 2 * C::BM - 1) / (2 * C::BM));
+  p.num_n_blocks = static_cast<int32_t>((pr.N + BN - 1) / BN);
+  p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
+  p.eps = pr.eps;
+  p.bias = pr.bias;
+  p.out = pr.out;
+  p.out_row_stride = pr.out_row_stride;
+  p.timeout_ns = wait_timeout_ns();
+  const int tiles = p.num_m_blocks * p.num_n_blocks;
+  const int pairs = tiles < pairs_avail ? tiles : pairs_avail;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
+  if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_pair", e);
+  return 0;
+}
+
+// Pair-tile width: minimise (pair tiles per pair) x BN over BN in {256, 224,
+// 192, 160, 128}; ties go to the wider tile (fewer W re-reads of x).
+int choose_pair_kernel(int64_t M, int64_t N, int pairs) {
+  const int64_t mb = (M + 255) / 256;
+  const int bns[5] = {256, 224, 192, 160, 128};
+  double best = 1e300;
+  int best_bn = 256;
+  for (int i = 0; i < 5; ++i) {
+    const int64_t tiles = mb * ((N + bns[i] - 1) / bns[i]);
+    const int64_t per_pair = (tiles + pairs - 1) / pairs;
+    const double cost = static_cast<double>(per_pair) * (bns[i] + 16);
+    if (cost < best - 1e-9) { best = cost; best_bn = bns[i]; }
+  }
+  return best_bn;
+}
+
+template <typename T>
+static int run_pair_t(const LinearProblem& pr, int bn, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_pair<T, 256, 6>(pr, s);
+    case 224: return launch_pair<T, 224, 6>(pr, s);
+    case 192: return launch_pair<T, 192, 6>(pr, s);
+    case 160: return launch_pair<T, 160, 6>(pr, s);
+    case 128: return launch_pair<T, 128, 8>(pr, s);
+    default: return set_error(FRN_ERR_INVALID_ARGUMENT, "unsupported pair tile width %d", bn);
+  }
+}
+
+int run_fused_linear_pair(const LinearProblem& pr, int bn, cudaStream_t s) {
+  if (pr.dtype == FRN_DTYPE_BF16) return run_pair_t<__nv_bfloat16>(pr, bn, s);
+  if (pr.dtype == FRN_DTYPE_F16) return run_pair_t<__half>(pr, bn, s);
+  return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+Linear supports bf16 and fp16 only");
+}
+
+}  // namespace frn

@@ -48,6 +48,9 @@ uint64_t wait_timeout_ns();
 
 int choose_prefill_kernel(int64_t M, int64_t N, int sms);
 int run_fused_linear_prefill(const LinearProblem& pr, int kernel, cudaStream_t s);
+// SM-pair (cta_group::2) kernel: `bn` is the pair tile width.
+int choose_pair_kernel(int64_t M, int64_t N, int pairs);
+int run_fused_linear_pair(const LinearProblem& pr, int bn, cudaStream_t s);
 
 int run_rmsnorm_normalize(int dtype, const void* x, int64_t xs, void* out, int64_t os,
                           const void* b, int64_t rows, int64_t h, int64_t n, float eps,

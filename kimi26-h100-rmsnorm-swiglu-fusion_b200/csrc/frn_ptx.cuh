@@ -47,37 +47,41 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or `hint_ns` elapses, instead of spinning and stealing
+// issue slots from the warps doing real work on the same scheduler.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity,
+                                              uint32_t hint_ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar_addr), "r"(parity)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 
+constexpr uint32_t kWaitHintNs = 200000u;  // 200 us per suspended try_wait
+
 // Waits for the phase of `bar` with the given parity to complete.  Gives up
-// after `timeout_ns` of wall time (checked every 256 polls), records the
-// failure in g_frn_device_error and in *abort_flag (shared), and returns
-// false.  Also returns false early if another role already aborted.
+// after `timeout_ns` of wall time, records the failure in g_frn_device_error
+// and in *abort_flag (shared), and returns false.  Also returns false early
+// if another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile uint32_t* abort_flag,
                                           uint64_t timeout_ns) {
   const uint32_t a = smem_addr(bar);
-  if (mbar_try_wait(a, parity)) return true;
-  uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > timeout_ns) {
-        *abort_flag = 1u;
-        atomicOr(&g_frn_device_error, kDevErrWaitTimeout);
-        return false;
-      }
+  if (mbar_try_wait(a, parity, kWaitHintNs)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait(a, parity, kWaitHintNs)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1u;
+      atomicOr(&g_frn_device_error, kDevErrWaitTimeout);
+      return false;
     }
   }
 }
@@ -190,6 +194,138 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- clusters / CTA pairs
+__device__ __forceinline__ uint32_t cluster_cta_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared variable in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of any CTA in the cluster (release at cluster scope:
+// orders every prior memory access of this thread, global stores included).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// Relaxed remote arrive: no memory ordering beyond the barrier itself.  Used
+// where the only thing to order is tcgen05 work, which the caller fences with
+// tcgen05.fence::before_thread_sync; avoids waiting for outstanding stores.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for barriers that receive arrivals from the peer CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile uint32_t* abort_flag,
+                                                  uint64_t timeout_ns) {
+  const uint32_t a = smem_addr(bar);
+  if (mbar_try_wait_cluster(a, parity, kWaitHintNs)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    if (mbar_try_wait_cluster(a, parity, kWaitHintNs)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1u;
+      atomicOr(&g_frn_device_error, kDevErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// Full cluster barrier (all threads of all CTAs), not warp-aligned.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// 2-D tiled TMA load for a CTA pair: data lands in this CTA's smem, the
+// transaction bytes are signalled on `bar_cluster_addr`, which may be the
+// mbarrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* m,
+                                                 uint32_t bar_cluster_addr, int32_t c0,
+                                                 int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_addr(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D(tmem, both CTAs) (+)= A(smem, both CTAs) * B(smem, both CTAs)^T with
+// M = 256 across the pair; issued by one thread of the even CTA.
+__device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at this offset in every CTA of `cta_mask` when
+// all prior tcgen05 ops of this thread (pair MMAs included) have completed.
+__device__ __forceinline__ void umma_commit_pair_mc(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_addr(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- descriptors

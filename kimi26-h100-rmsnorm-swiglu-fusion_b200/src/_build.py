@@ -33,6 +33,7 @@ LIB_PATH = os.path.join(LIB_DIR, LIB_NAME)
 CU_SOURCES = [
     "frn_capi.cu",
     "frn_fused_linear.cu",
+    "frn_fused_linear_pair.cu",
     "frn_normalize.cu",
 ]
 HEADERS = ["frn_ptx.cuh", "frn_internal.h"]

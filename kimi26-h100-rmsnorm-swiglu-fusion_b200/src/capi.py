@@ -30,6 +30,11 @@ FRN_KERNEL_TILE_N128 = 1
 FRN_KERNEL_TILE_N192 = 2
 FRN_KERNEL_TILE_N256 = 3
 FRN_KERNEL_DECODE = 4
+FRN_KERNEL_PAIR_N128 = 5
+FRN_KERNEL_PAIR_N160 = 6
+FRN_KERNEL_PAIR_N192 = 7
+FRN_KERNEL_PAIR_N224 = 8
+FRN_KERNEL_PAIR_N256 = 9
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {

@@ -51,8 +51,12 @@ def test_baseline_configs_full_size(config):
     _check(out, x, gamma, W, W_new, b, config)
 
 
-@pytest.mark.parametrize("kernel", [capi.FRN_KERNEL_TILE_N128, capi.FRN_KERNEL_TILE_N192,
-                                    capi.FRN_KERNEL_TILE_N256])
+ALL_KERNELS = [capi.FRN_KERNEL_TILE_N128, capi.FRN_KERNEL_TILE_N192, capi.FRN_KERNEL_TILE_N256,
+               capi.FRN_KERNEL_PAIR_N128, capi.FRN_KERNEL_PAIR_N160, capi.FRN_KERNEL_PAIR_N192,
+               capi.FRN_KERNEL_PAIR_N224, capi.FRN_KERNEL_PAIR_N256]
+
+
+@pytest.mark.parametrize("kernel", ALL_KERNELS)
 @pytest.mark.parametrize("shape", [(512, 1536, 12288), (512, 512, 16384), (300, 1536, 1000),
                                    (129, 72, 264)])
 def test_every_tile_width(kernel, shape):
@@ -104,6 +108,18 @@ def test_fp16():
     torch.cuda.synchronize()
     assert out.dtype == torch.float16
     _check(out, x, gamma, W, W_new, b, "fp16")
+
+
+@pytest.mark.parametrize("kernel", ALL_KERNELS)
+def test_strided_fp16_bias_every_kernel(kernel):
+    M, K, N = 384, 576, 1040
+    x, gamma, W, W_new, b = _inputs(M, K, N, seed=12, dtype=torch.float16, bias=True)
+    full = torch.zeros(M, K + 64, dtype=torch.float16)
+    full[:, :K] = x
+    out = capi.fused_rmsnorm_linear(full.to(DEV)[:, :K], W_new.to(DEV), b.to(DEV), orc.EPS,
+                                    kernel=kernel)
+    torch.cuda.synchronize()
+    _check(out, x, gamma, W, W_new, b, f"kernel{kernel} strided fp16")
 
 
 def test_deterministic_bits():
