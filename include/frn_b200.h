@@ -46,7 +46,7 @@ extern "C" {
 #define FRN_DTYPE_BF16  2
 
 /* ---- kernel selection for frn_fused_rmsnorm_linear_ex ------------------ */
-#define FRN_KERNEL_AUTO         0  /* pick by (M, N, K)                       */
+#define FRN_KERNEL_AUTO         0  /* DECODE for M <= 128, else PAIR_AUTO     */
 #define FRN_KERNEL_TILE_N128    1  /* one SM per 128x128 tile                 */
 #define FRN_KERNEL_TILE_N192    2  /* one SM per 128x192 tile                 */
 #define FRN_KERNEL_TILE_N256    3  /* one SM per 128x256 tile                 */
@@ -56,6 +56,7 @@ extern "C" {
 #define FRN_KERNEL_PAIR_N192    7  /* SM pair per 256x192 tile                */
 #define FRN_KERNEL_PAIR_N224    8  /* SM pair per 256x224 tile                */
 #define FRN_KERNEL_PAIR_N256    9  /* SM pair per 256x256 tile                */
+#define FRN_KERNEL_PAIR_AUTO   10  /* SM pair, tile width chosen by (M, N)    */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */

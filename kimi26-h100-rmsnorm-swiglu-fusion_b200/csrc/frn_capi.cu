@@ -179,13 +179,21 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (kernel == FRN_KERNEL_AUTO)
-    return run_fused_linear_pair(p, choose_pair_kernel(M, N, sm_count(dev) / 2), s);
+  const int sms = sm_count(dev);
+  if (kernel == FRN_KERNEL_AUTO) kernel = (M <= 128) ? FRN_KERNEL_DECODE : FRN_KERNEL_PAIR_AUTO;
+  if (kernel == FRN_KERNEL_PAIR_AUTO)
+    return run_fused_linear_pair(p, choose_pair_kernel(M, N, sms / 2), s);
   if (kernel >= FRN_KERNEL_TILE_N128 && kernel <= FRN_KERNEL_TILE_N256)
     return run_fused_linear_prefill(p, kernel, s);
   if (kernel >= FRN_KERNEL_PAIR_N128 && kernel <= FRN_KERNEL_PAIR_N256) {
     static const int bns[5] = {128, 160, 192, 224, 256};
     return run_fused_linear_pair(p, bns[kernel - FRN_KERNEL_PAIR_N128], s);
+  }
+  if (kernel == FRN_KERNEL_DECODE) {
+    if (M > 128)
+      return set_error(FRN_ERR_UNSUPPORTED, "the decode kernel takes M <= 128 (got %lld)",
+                       (long long)M);
+    return run_fused_linear_decode(p, choose_decode_split(N, K, sms), s);
   }
   return set_error(FRN_ERR_UNSUPPORTED, "kernel id %d not available", kernel);
 }

@@ -1,0 +1,433 @@
+// frn_decode.cu -- fused RMSNorm -> Linear for decode batches (M <= 128).
+//
+// With few tokens the op is a weight stream: W [N, K] dominates the bytes
+// (Llama-3-8B QKV: 50 MB of W against 8 KB - 1 MB of x), so the kernel is
+// built to keep ~all SMs pulling W from HBM:
+//
+//   swap-AB   D^T[n, t] = W[n, :] . x[t, :]: a 128-row W tile is the UMMA M
+//             operand, the MP (16/32/64/128) padded tokens are UMMA N, the
+//             fp32 accumulator sits in TMEM (lane = W row, column = token).
+//   split-K   the CTAs of one thread-block cluster (S <= 8) share a W tile and
+//             each streams 1/S of K, so N/128 * S CTAs cover the SMs.
+//   reduce    each CTA writes its fp32 partial D^T and its partial sum of x^2
+//             per token into its own shared memory; after a cluster barrier,
+//             CTA r reduces tokens t = r, r+S, ... by reading the S partials
+//             through distributed shared memory in rank order (deterministic,
+//             no atomics, no global workspace), applies
+//             inv_rms[t] = rsqrt(sum_s ss_s[t] / K + eps) and b[n], and stores
+//             out[t, n0 .. n0+127] as coalesced rows.
+//
+// Roles: warps 0-3 epilogue (TMEM lanes -> partial buffer) and reduction,
+// warps 4-7 TMA producers (W / x over even / odd stages), warp 8 MMA issuer +
+// TMEM owner, warps 9-12 RMS (thread t sums x[t, k-range]^2 from x stages).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "frn_internal.h"
+#include "frn_ptx.cuh"
+
+namespace frn {
+
+struct DecodeParams {
+  int32_t M, N, K;
+  int32_t num_k_blocks;
+  int32_t split;  // CTAs per cluster (k-splits)
+  float eps;
+  const void* bias;
+  void* out;
+  int64_t out_row_stride;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float2 ld_shared_cluster_f32x2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr)
+               : "memory");
+  return v;
+}
+
+template <int MP, int STAGES>
+struct DecodeCfg {
+  static constexpr int BM = 128;  // W rows per tile
+  static constexpr int BK = 64;
+  static constexpr int W_BYTES = BM * BK * 2;
+  static constexpr int X_BYTES = MP * BK * 2;
+  static constexpr int STAGE_TX = W_BYTES + X_BYTES;
+  static constexpr uint32_t TMEM_COLS = MP < 32 ? 32u : static_cast<uint32_t>(MP);
+  static constexpr int OFF_W = 0;
+  static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
+  static constexpr int PART_BYTES = MP * BM * 4;  // fp32 partial D, [token][w row]
+  static constexpr int PIPE_BYTES = STAGES * (W_BYTES + X_BYTES);
+  static constexpr int OFF_SS = (PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES);
+  static constexpr int OFF_BAR = OFF_SS + 128 * 4;
+  static constexpr int NUM_BARS = 2 * STAGES + 2;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  // warps 4-7: producers (W | x) x (even | odd stages); 8: MMA; 9-12: RMS
+  static constexpr int WARP_PROD0 = 4, WARP_MMA = 8, WARP_RMS0 = 9;
+  static constexpr int THREADS = 32 * 13;
+  static_assert(STAGES % 2 == 0, "stages are split between two producers per operand");
+  static_assert(MP % 16 == 0 && MP >= 16 && MP <= 128, "MP");
+  static_assert(X_BYTES % 1024 == 0, "x stages must stay 1024-aligned");
+  // The partial buffer may only overlap the W stages (read by the MMA alone),
+  // never the x stages, which RMS warps can still be reading.
+  static_assert(PART_BYTES <= STAGES * W_BYTES, "partial buffer overlaps the x stages");
+  static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
+};
+
+template <typename T, int MP, int STAGES>
+__global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
+    fused_rmsnorm_linear_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                                       const __grid_constant__ CUtensorMap tmap_x,
+                                       const DecodeParams p) {
+  using C = DecodeCfg<MP, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* drain = tmem_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* part = reinterpret_cast<float*>(smem);  // reuses the pipeline buffers
+  float* ssq = reinterpret_cast<float*>(smem + C::OFF_SS);
+
+  const uint32_t warp = warp_id_in_cta();
+  const uint32_t lane = threadIdx.x & 31u;
+  const int S = p.split;
+  const uint32_t rank = cluster_cta_rank();
+  const int tile = static_cast<int>(blockIdx.x) / S;
+  const int n0 = tile * C::BM;
+  // k-blocks [kb_begin, kb_end) of this split (first splits take the remainder)
+  const int base = p.num_k_blocks / S, rem = p.num_k_blocks % S;
+  const int kb_begin = static_cast<int>(rank) * base + (static_cast<int>(rank) < rem ? rank : rem);
+  const int nkb = base + (static_cast<int>(rank) < rem ? 1 : 0);
+  const uint64_t to = p.timeout_ns;
+
+  if (warp == C::WARP_PROD0 && lane == 0) {
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_x);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 2);       // W producer + x producer arrive with tx
+      mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 RMS warps
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_mbarrier_init();
+  }
+  if (warp == C::WARP_MMA) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp >= C::WARP_PROD0 && warp < C::WARP_PROD0 + 4) {
+    // Four issuing threads (a single thread keeps only a few bulk-tensor
+    // loads in flight): W / x, each over even / odd stages.
+    if (lane == 0) {
+      griddep_wait();
+      const uint32_t pid = warp - C::WARP_PROD0;
+      const bool is_w = (pid & 1u) == 0;
+      const uint32_t parity_sel = pid >> 1;
+      uint32_t stage = 0, phase = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if ((stage & 1u) != parity_sel) {
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          continue;
+        }
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, to)) break;
+        const int kc = (kb_begin + i) * C::BK;
+        if (is_w) {
+          mbar_arrive_expect_tx(&full[stage], C::W_BYTES);
+          tma_load_2d(smem + C::OFF_W + stage * C::W_BYTES, &tmap_w, &full[stage], kc, n0);
+        } else {
+          mbar_arrive_expect_tx(&full[stage], C::X_BYTES);
+          tma_load_2d(smem + C::OFF_X + stage * C::X_BYTES, &tmap_x, &full[stage], kc, 0);
+        }
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == C::WARP_MMA) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_f16(Elem16<T>::kUmmaFormat, C::BM, MP);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t w_addr = smem_addr(smem + C::OFF_W + stage * C::W_BYTES);
+        const uint32_t x_addr = smem_addr(smem + C::OFF_X + stage * C::X_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BK / 16; ++k)
+          umma_f16_ss(tmem_base, make_smem_desc_k_sw128(w_addr + k * 32),
+                      make_smem_desc_k_sw128(x_addr + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (ok) umma_commit(tmem_full);
+      umma_commit(drain);
+      uint32_t zero = 0;
+      mbar_wait(drain, 0, &zero, to);
+    }
+  } else if (warp >= C::WARP_RMS0) {
+    // Thread t sums x[t, k-range]^2 straight from the x stages.
+    const int t = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;
+    uint32_t stage = 0, phase = 0;
+    float ss0 = 0.f, ss1 = 0.f;
+    for (int i = 0; i < nkb; ++i) {
+      if (!mbar_wait(&full[stage], phase, abort_flag, to)) break;
+      if (t < MP) {
+        const uint8_t* row = smem + C::OFF_X + stage * C::X_BYTES + t * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (t & 7)) << 4));
+          const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
+          const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
+          ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
+          ss0 = fmaf(f1.x, f1.x, ss0); ss1 = fmaf(f1.y, f1.y, ss1);
+          ss0 = fmaf(f2.x, f2.x, ss0); ss1 = fmaf(f2.y, f2.y, ss1);
+          ss0 = fmaf(f3.x, f3.x, ss0); ss1 = fmaf(f3.y, f3.y, ss1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+    }
+    // Published after the cluster barrier below, once the pipeline is idle.
+    if (t < MP) ssq[t] = ss0 + ss1;
+  } else {
+    // Epilogue warps 0-3: accumulator lanes -> partial buffer [token][w row].
+    // The pipeline buffers are reused, so wait until every MMA is done.
+    const uint32_t q = warp;
+    if (mbar_wait(tmem_full, 0, abort_flag, to)) {
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((q * 32u) << 16);
+      const int wrow = static_cast<int>(q * 32 + lane);
+#pragma unroll 1
+      for (int c = 0; c < MP / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(taddr + c * 16, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) part[(c * 16 + e) * C::BM + wrow] = __uint_as_float(v[e]);
+      }
+    }
+  }
+
+  // All partials (and x^2 sums) of the cluster are in shared memory.
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+
+  if (warp < 4 && !*abort_flag) {
+    // CTA `rank` reduces tokens rank, rank+S, ...: 64 threads per token, each
+    // owning W rows pr, pr+1 of the tile, two tokens in flight.
+    griddep_wait();
+    const int pr = static_cast<int>(threadIdx.x & 63u) * 2;
+    const int tsub = static_cast<int>(threadIdx.x >> 6);
+    const bool has_bias = p.bias != nullptr;
+    float b0 = 0.f, b1 = 0.f;
+    if (has_bias && n0 + pr < p.N) {
+      const float2 bb = pair_to_float2<T>(*reinterpret_cast<const uint32_t*>(
+          static_cast<const T*>(p.bias) + n0 + pr));
+      b0 = bb.x;
+      b1 = bb.y;
+    }
+    const uint32_t part_local = smem_addr(part);
+    const uint32_t ssq_local = smem_addr(ssq);
+    // Tokens in batches of kBatch: every distributed-shared-memory load of a
+    // batch is issued before any is consumed (remote loads are slow).
+    constexpr int kBatch = 4;
+    const int t_first = static_cast<int>(rank) + S * tsub;
+    const int t_end = p.M < MP ? p.M : MP;
+    for (int t0 = t_first; t0 < t_end; t0 += 2 * S * kBatch) {
+      float2 acc[kBatch];
+      float ss[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) { acc[j] = make_float2(0.f, 0.f); ss[j] = 0.f; }
+      for (int s = 0; s < S; ++s) {  // fixed rank order: deterministic sums
+        const uint32_t part_s = mapa_shared(part_local, s);
+        const uint32_t ssq_s = mapa_shared(ssq_local, s);
+        float2 v[kBatch];
+        float q[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int t = t0 + j * 2 * S;
+          const int tc = t < t_end ? t : t_first;  // clamp: loads stay in bounds
+          v[j] = ld_shared_cluster_f32x2(part_s + (tc * C::BM + pr) * 4);
+          q[j] = ld_shared_cluster_f32(ssq_s + tc * 4);
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          acc[j].x += v[j].x;
+          acc[j].y += v[j].y;
+          ss[j] += q[j];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int t = t0 + j * 2 * S;
+        if (t < t_end && n0 + pr < p.N) {
+          const float r = rsqrtf(ss[j] / static_cast<float>(p.K) + p.eps);
+          T* o = static_cast<T*>(p.out) + static_cast<int64_t>(t) * p.out_row_stride + n0 + pr;
+          *reinterpret_cast<uint32_t*>(o) = float2_to_pair<T>(acc[j].x * r + b0, acc[j].y * r + b1);
+        }
+      }
+    }
+  }
+
+  // Nobody leaves while a peer may still read its shared memory.
+  __syncwarp();
+  cluster_sync_all();
+  if (*abort_flag) __nanosleep(20000);
+  if (warp == C::WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+// Clusters of `split` CTAs of this kernel that can be resident at once.
+template <typename T, int MP, int STAGES>
+static int max_clusters(int split) {
+  using C = DecodeCfg<MP, STAGES>;
+  cudaLaunchConfig_t qc = {};
+  qc.gridDim = dim3(split * 64);
+  qc.blockDim = dim3(C::THREADS);
+  qc.dynamicSmemBytes = C::SMEM_BYTES;
+  cudaLaunchAttribute qa[1];
+  qa[0].id = cudaLaunchAttributeClusterDimension;
+  qa[0].val.clusterDim.x = split;
+  qa[0].val.clusterDim.y = 1;
+  qa[0].val.clusterDim.z = 1;
+  qc.attrs = qa;
+  qc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fused_rmsnorm_linear_decode_kernel<T, MP, STAGES>, &qc) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <typename T, int MP, int STAGES>
+static int launch_decode(const LinearProblem& pr, int split, cudaStream_t stream) {
+  using C = DecodeCfg<MP, STAGES>;
+  auto kern = fused_rmsnorm_linear_decode_kernel<T, MP, STAGES>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  static bool attr_set[kMaxDevices] = {};
+  if (dev < kMaxDevices && !attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(decode kernel)", e);
+    attr_set[dev] = true;
+  }
+  // Largest k-split (<= the requested one) whose clusters all fit in one
+  // wave: a second wave would double the time of this weight stream.
+  {
+    static int fits[kMaxDevices][9] = {};
+    const int64_t tiles64 = (pr.N + C::BM - 1) / C::BM;
+    while (split > 1) {
+      int& f = fits[dev < kMaxDevices ? dev : 0][split];
+      if (f == 0) f = max_clusters<T, MP, STAGES>(split) + 1;  // +1: 0 means "not queried"
+      if (tiles64 <= f - 1) break;
+      --split;
+    }
+  }
+  const CUtensorMapDataType dt = Elem16<T>::kTmaType;
+  CUtensorMap tw, tx;
+  int rc = encode_tmap_2d(&tw, dt, 2, pr.w, pr.K, pr.N, pr.w_row_stride, C::BK, C::BM,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tx, dt, 2, pr.x, pr.K, pr.M, pr.x_row_stride, C::BK, MP,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  DecodeParams p;
+  p.M = static_cast<int32_t>(pr.M);
+  p.N = static_cast<int32_t>(pr.N);
+  p.K = static_cast<int32_t>(pr.K);
+  p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
+  p.split = split;
+  p.eps = pr.eps;
+  p.bias = pr.bias;
+  p.out = pr.out;
+  p.out_row_stride = pr.out_row_stride;
+  p.timeout_ns = wait_timeout_ns();
+  const int tiles = static_cast<int>((pr.N + C::BM - 1) / C::BM);
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * split);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = split;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, p);
+  if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_decode", e);
+  return 0;
+}
+
+// k-split per W tile: as many CTAs per tile as fit one wave (<= 8, the
+// portable cluster size) without splits shorter than 4 k-blocks.
+int choose_decode_split(int64_t N, int64_t K, int sms) {
+  const int64_t tiles = (N + 127) / 128;
+  const int64_t nkb = (K + 63) / 64;
+  int s = static_cast<int>(sms / (tiles > 0 ? tiles : 1));
+  if (s > 8) s = 8;
+  while (s > 1 && nkb / s < 4) --s;
+  return s < 1 ? 1 : s;
+}
+
+template <typename T>
+static int run_decode_t(const LinearProblem& pr, int split, cudaStream_t s) {
+  if (pr.M <= 16) return launch_decode<T, 16, 8>(pr, split, s);
+  if (pr.M <= 32) return launch_decode<T, 32, 8>(pr, split, s);
+  if (pr.M <= 64) return launch_decode<T, 64, 6>(pr, split, s);
+  if (pr.M <= 128) return launch_decode<T, 128, 6>(pr, split, s);
+  return set_error(FRN_ERR_UNSUPPORTED, "decode kernel takes M <= 128 (got %lld)",
+                   static_cast<long long>(pr.M));
+}
+
+int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s) {
+  if (pr.dtype == FRN_DTYPE_BF16) return run_decode_t<__nv_bfloat16>(pr, split, s);
+  if (pr.dtype == FRN_DTYPE_F16) return run_decode_t<__half>(pr, split, s);
+  return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+Linear supports bf16 and fp16 only");
+}
+
+}  // namespace frn

@@ -51,6 +51,9 @@ int run_fused_linear_prefill(const LinearProblem& pr, int kernel, cudaStream_t s
 // SM-pair (cta_group::2) kernel: `bn` is the pair tile width.
 int choose_pair_kernel(int64_t M, int64_t N, int pairs);
 int run_fused_linear_pair(const LinearProblem& pr, int bn, cudaStream_t s);
+// Decode (M <= 128) swap-AB kernel, `split` CTAs per cluster along K.
+int choose_decode_split(int64_t N, int64_t K, int sms);
+int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s);
 
 int run_rmsnorm_normalize(int dtype, const void* x, int64_t xs, void* out, int64_t os,
                           const void* b, int64_t rows, int64_t h, int64_t n, float eps,

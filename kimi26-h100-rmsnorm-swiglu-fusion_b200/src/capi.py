@@ -35,6 +35,7 @@ FRN_KERNEL_PAIR_N160 = 6
 FRN_KERNEL_PAIR_N192 = 7
 FRN_KERNEL_PAIR_N224 = 8
 FRN_KERNEL_PAIR_N256 = 9
+FRN_KERNEL_PAIR_AUTO = 10
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {

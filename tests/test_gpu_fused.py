@@ -122,6 +122,39 @@ def test_strided_fp16_bias_every_kernel(kernel):
     _check(out, x, gamma, W, W_new, b, f"kernel{kernel} strided fp16")
 
 
+@pytest.mark.parametrize("M", [1, 2, 7, 8, 16, 17, 32, 33, 64, 100, 128])
+@pytest.mark.parametrize("K,N", [(4096, 6144), (512, 16384), (72, 136), (1536, 1000)])
+def test_decode_kernel(M, K, N):
+    """Swap-AB split-K cluster kernel for M <= 128 (the Llama-3-8B QKV decode
+    sweep is K=4096, N=6144), against the oracle; bias on odd M."""
+    x, gamma, W, W_new, b = _inputs(M, K, N, seed=M + 3 * K + N, bias=(M % 2 == 1))
+    bd = b.to(DEV) if b is not None else None
+    out = capi.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), bd, orc.EPS,
+                                    kernel=capi.FRN_KERNEL_DECODE)
+    torch.cuda.synchronize()
+    _check(out, x, gamma, W, W_new, b, f"decode M{M} K{K} N{N}")
+
+
+def test_decode_strided_fp16_and_determinism():
+    M, K, N = 24, 4096, 6144
+    x, gamma, W, W_new, b = _inputs(M, K, N, seed=31, dtype=torch.float16, bias=True)
+    full = torch.zeros(M, K + 64, dtype=torch.float16)
+    full[:, :K] = x
+    xs, wd, bd = full.to(DEV)[:, :K], W_new.to(DEV), b.to(DEV)
+    o1 = capi.fused_rmsnorm_linear(xs, wd, bd, orc.EPS, kernel=capi.FRN_KERNEL_DECODE)
+    o2 = capi.fused_rmsnorm_linear(xs, wd, bd, orc.EPS, kernel=capi.FRN_KERNEL_DECODE)
+    torch.cuda.synchronize()
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+    _check(o1, x, gamma, W, W_new, b, "decode strided fp16")
+
+
+def test_decode_rejects_large_m():
+    x = torch.zeros(129, 64, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(64, 64, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(capi.FrnError):
+        capi.fused_rmsnorm_linear(x, w, None, orc.EPS, kernel=capi.FRN_KERNEL_DECODE)
+
+
 def test_deterministic_bits():
     M, K, N = 512, 1536, 12288
     x, gamma, W, W_new, b = _inputs(M, K, N, seed=9)
