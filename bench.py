@@ -467,7 +467,42 @@ def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
                      "speedup_vs_unfused": round(t_base / t_ours, 3)}
         del rot
         torch.cuda.empty_cache()
+    res["int8_q_b"] = sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps)
     return res
+
+
+def sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps):
+    """int8-weight q_b at 2048 tokens: ours vs the reference's quantization-
+    aware GPU path (dequantize W to bf16, then F.linear(x * bf16(inv_rms), W))."""
+    import torch
+    import torch.nn.functional as F
+
+    M, K, N = 2048, 1536, 12288
+    sets = []
+    for s in range(4):
+        x, gamma, W = gpu_inputs(M, K, N, 500 + s, device)
+        q, sc = denominator_cuda.quantize_int8_per_channel(W * gamma)
+        sets.append((x, q, sc, torch.empty(M, N, dtype=torch.bfloat16, device=device)))
+    ours = [(lambda t=t: denominator_cuda.fused_rmsnorm_linear_w8(t[0], t[1], t[2], None, EPS, t[3]))
+            for t in sets]
+
+    def ref_path(t):
+        x, q, sc, _ = t
+        w = (q.float() * sc.float().unsqueeze(1)).to(torch.bfloat16)
+        variance = x.float().pow(2).mean(dim=-1, keepdim=True)
+        return F.linear(x * torch.rsqrt(variance + EPS).to(torch.bfloat16), w)
+
+    base = [(lambda t=t: ref_path(t)) for t in sets]
+    n = 16
+    t_ours = time_steps(ours, n, 4) * 1e3 / n
+    t_base = time_steps(base, n, 4) * 1e3 / n
+    fl = flops_of(M, K, N)
+    by = M * K * 2 + N * K + N * 4 + M * N * 2
+    roof_us = max(fl / (tflops_peak * 1e12), by / (hbm_gbs * 1e9)) * 1e6
+    return {"us_per_call": round(t_ours, 3), "tflops": round(fl / t_ours / 1e6, 1),
+            "roofline_us": round(roof_us, 3), "frac_of_roofline": round(roof_us / t_ours, 3),
+            "reference_dequant_linear_us": round(t_base, 3),
+            "speedup_vs_reference_path": round(t_base / t_ours, 3)}
 
 
 def main():

@@ -122,6 +122,36 @@ int frn_fused_rmsnorm_linear_ex(int dtype,
                                 int kernel, void* stream);
 
 /*
+ * Fused RMSNorm -> Linear with int8 weights:
+ *     out[M,N] = round(inv_rms[m] * w_scale[n] * (x[M,K] . wq[N,K]^T) + bias[N])
+ * dtype (FRN_DTYPE_BF16 / FRN_DTYPE_F16) applies to x, bias and out; wq is
+ * int8 row-major (row stride in bytes, a multiple of 16), w_scale fp32 [N]
+ * (16-byte aligned).  The int8 bytes are what crosses HBM; they are widened
+ * to the x type in shared memory inside the GEMM mainloop.
+ * Replaces dequantize_int8 + F.linear(x * bf16(inv_rms), W_deq) of the
+ * reference's quantization-aware path (src/benchmark_kimi26_quantized.py:38-39,
+ * :102-106), which materialises the bf16 weight on every call.
+ */
+int frn_fused_rmsnorm_linear_w8(int dtype,
+                                const void* x, int64_t M, int64_t K,
+                                int64_t x_row_stride,
+                                const int8_t* wq, int64_t N, int64_t wq_row_stride,
+                                const float* w_scale, const void* bias, float eps,
+                                void* out, int64_t out_row_stride, void* stream);
+
+/*
+ * Symmetric per-output-channel int8 quantization of a (gamma-folded) weight
+ * w[N,K] (dtype fp32 / fp16 / bf16):
+ *     scale[n] = max(max_k |w[n,k]|, 1e-8) / 127        (fp32)
+ *     q[n,k]   = clamp(round_half_even(w[n,k] / scale[n]), -127, 127)
+ * Same numbers as quantize_int8_per_output_channel
+ * (reference src/benchmark_kimi26_quantized.py:30-35), on the GPU.
+ */
+int frn_quantize_int8_per_channel(int dtype, const void* w, int64_t N, int64_t K,
+                                  int64_t w_row_stride, int8_t* q, int64_t q_row_stride,
+                                  float* scale, void* stream);
+
+/*
  * Reads (and optionally clears) the device error word of `device`, which
  * kernels set when a bounded wait expires instead of hanging.  Synchronous
  * with respect to the device's legacy default stream.

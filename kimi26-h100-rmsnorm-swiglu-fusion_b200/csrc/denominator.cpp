@@ -118,6 +118,60 @@ at::Tensor fused_rmsnorm_linear(const at::Tensor& x_in, const at::Tensor& w,
   return o;
 }
 
+at::Tensor fused_rmsnorm_linear_w8(const at::Tensor& x_in, const at::Tensor& qweight,
+                                   const at::Tensor& w_scale, const c10::optional<at::Tensor>& b_new,
+                                   double eps, c10::optional<at::Tensor> out) {
+  TORCH_CHECK(x_in.dim() == 2 && qweight.dim() == 2, "x and qweight must be 2D");
+  TORCH_CHECK(x_in.is_cuda() && qweight.is_cuda() && w_scale.is_cuda() &&
+                  (!b_new || b_new->is_cuda()),
+              "All tensors must be on CUDA");
+  TORCH_CHECK(x_in.scalar_type() == at::kBFloat16 || x_in.scalar_type() == at::kHalf,
+              "fused_rmsnorm_linear_w8 takes bf16 or fp16 x");
+  TORCH_CHECK(qweight.scalar_type() == at::kChar, "qweight must be int8");
+  TORCH_CHECK(w_scale.scalar_type() == at::kFloat && w_scale.numel() == qweight.size(0),
+              "w_scale must be fp32 with qweight.size(0) elements");
+  TORCH_CHECK(x_in.size(1) == qweight.size(1), "x.size(1) != qweight.size(1)");
+  const at::Tensor x = (x_in.stride(1) == 1) ? x_in : x_in.contiguous();
+  const at::Tensor q = qweight.stride(1) == 1 ? qweight : qweight.contiguous();
+  const at::Tensor sc = w_scale.contiguous();
+  const int64_t M = x.size(0), K = x.size(1), N = q.size(0);
+  at::Tensor b;
+  const void* bptr = nullptr;
+  if (b_new && b_new->defined()) {
+    TORCH_CHECK(b_new->scalar_type() == x.scalar_type() && b_new->numel() == N,
+                "b_new must share x's dtype and have qweight.size(0) elements");
+    b = b_new->contiguous();
+    bptr = b.data_ptr();
+  }
+  at::Tensor o = (out && out->defined()) ? *out : at::empty({M, N}, x.options());
+  TORCH_CHECK(o.dim() == 2 && o.size(0) == M && o.size(1) == N && o.stride(1) == 1,
+              "out must be [M, N] with unit inner stride");
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(frn_fused_rmsnorm_linear_w8(dtype_code(x), x.data_ptr(), M, K, x.stride(0),
+                                       static_cast<const int8_t*>(q.data_ptr()), N, q.stride(0),
+                                       sc.data_ptr<float>(), bptr, static_cast<float>(eps),
+                                       o.data_ptr(), o.stride(0), stream_of(x)),
+           "fused_rmsnorm_linear_w8");
+  return o;
+}
+
+std::tuple<at::Tensor, at::Tensor> quantize_int8_per_channel(const at::Tensor& w_in) {
+  TORCH_CHECK(w_in.dim() == 2, "weight must be 2D");
+  TORCH_CHECK(w_in.is_cuda(), "All tensors must be on CUDA");
+  const int dt = dtype_code(w_in);
+  TORCH_CHECK(dt >= 0, "weight must be fp32, fp16 or bf16");
+  const at::Tensor w = w_in.stride(1) == 1 ? w_in : w_in.contiguous();
+  const int64_t N = w.size(0), K = w.size(1);
+  at::Tensor q = at::empty({N, K}, w.options().dtype(at::kChar));
+  at::Tensor sc = at::empty({N}, w.options().dtype(at::kFloat));
+  const c10::cuda::CUDAGuard guard(w.device());
+  check_rc(frn_quantize_int8_per_channel(dt, w.data_ptr(), N, K, w.stride(0),
+                                         static_cast<int8_t*>(q.data_ptr()), K,
+                                         sc.data_ptr<float>(), stream_of(w)),
+           "quantize_int8_per_channel");
+  return {q, sc};
+}
+
 int64_t device_error(int64_t device, bool clear) {
   uint32_t flags = 0;
   check_rc(frn_device_error(static_cast<int>(device), &flags, clear ? 1 : 0), "device_error");
@@ -158,6 +212,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "out = rsqrt(mean(x^2)+eps)[:,None] * (x @ W_fused.T) + b_new, one tcgen05 launch",
         py::arg("x"), py::arg("W_fused"), py::arg("b_new") = py::none(), py::arg("eps") = 1e-6,
         py::arg("out") = py::none(), py::arg("kernel") = 0);
+  m.def("fused_rmsnorm_linear_w8", &fused_rmsnorm_linear_w8,
+        "int8 weights: rsqrt(mean(x^2)+eps)[:,None] * w_scale * (x @ qweight.T) + b_new",
+        py::arg("x"), py::arg("qweight"), py::arg("w_scale"), py::arg("b_new") = py::none(),
+        py::arg("eps") = 1e-6, py::arg("out") = py::none());
+  m.def("quantize_int8_per_channel", &quantize_int8_per_channel,
+        "Symmetric per-output-channel int8 quantization on the GPU -> (qweight, w_scale)",
+        py::arg("weight"));
   m.def("device_error", &device_error, "Read (and optionally clear) the device error word",
         py::arg("device") = 0, py::arg("clear") = false);
   m.def("compute_denominator", &compute_denominator, "LayerNorm path: not implemented",

@@ -207,6 +207,50 @@ int frn_fused_rmsnorm_linear(int dtype, const void* x, int64_t M, int64_t K, int
                                      FRN_KERNEL_AUTO, stream);
 }
 
+int frn_fused_rmsnorm_linear_w8(int dtype, const void* x, int64_t M, int64_t K,
+                                int64_t x_row_stride, const int8_t* wq, int64_t N,
+                                int64_t wq_row_stride, const float* w_scale, const void* bias,
+                                float eps, void* out, int64_t out_row_stride, void* stream) {
+  if (dtype != FRN_DTYPE_BF16 && dtype != FRN_DTYPE_F16)
+    return set_error(FRN_ERR_UNSUPPORTED, "int8-weight RMSNorm+Linear takes bf16 or fp16 x");
+  if (M < 0 || N <= 0 || K <= 0)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "bad shape M=%lld N=%lld K=%lld", (long long)M,
+                     (long long)N, (long long)K);
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL)
+    return set_error(FRN_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
+  if (M == 0) return FRN_OK;
+  if (!x || !wq || !w_scale || !out)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "x, wq, w_scale and out must be non-null");
+  if (x_row_stride < K || wq_row_stride < K || out_row_stride < N)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "row strides must be >= row lengths");
+  if (K % 16 || N % 8 || x_row_stride % 8 || out_row_stride % 8 || wq_row_stride % 16)
+    return set_error(FRN_ERR_MISALIGNED,
+                     "K must be a multiple of 16, N of 8; x/out row strides multiples of 8 "
+                     "elements, wq row stride a multiple of 16 bytes");
+  if (!aligned16(x) || !aligned16(wq) || !aligned16(w_scale) || !aligned16(out) ||
+      (bias && !aligned16(bias)))
+    return set_error(FRN_ERR_MISALIGNED, "x, wq, w_scale, bias and out must be 16-byte aligned");
+  W8Problem p{dtype, x, M, K, x_row_stride, wq, N, wq_row_stride, w_scale, bias, eps, out,
+              out_row_stride};
+  return run_fused_linear_w8(p, static_cast<cudaStream_t>(stream));
+}
+
+int frn_quantize_int8_per_channel(int dtype, const void* w, int64_t N, int64_t K,
+                                  int64_t w_row_stride, int8_t* q, int64_t q_row_stride,
+                                  float* scale, void* stream) {
+  if (dtype != FRN_DTYPE_F32 && dtype != FRN_DTYPE_F16 && dtype != FRN_DTYPE_BF16)
+    return set_error(FRN_ERR_UNSUPPORTED, "quantize: weight dtype must be fp32, fp16 or bf16");
+  if (N < 0 || K <= 0 || w_row_stride < K || q_row_stride < K)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "quantize: bad shape or strides");
+  if (N == 0) return FRN_OK;
+  if (!w || !q || !scale)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "quantize: w, q and scale must be non-null");
+  if (N > 0x7fffffffLL || K > 0x7fffffffLL)
+    return set_error(FRN_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
+  return run_quantize_int8(dtype, w, N, K, w_row_stride, q, q_row_stride, scale,
+                           static_cast<cudaStream_t>(stream));
+}
+
 int frn_device_error(int device, uint32_t* flags, int clear) {
   if (!flags) return set_error(FRN_ERR_INVALID_ARGUMENT, "flags must be non-null");
   int prev = 0;

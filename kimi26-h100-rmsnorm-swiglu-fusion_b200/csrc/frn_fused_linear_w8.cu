@@ -1,0 +1,527 @@
+// frn_fused_linear_w8.cu -- fused RMSNorm -> Linear with int8 weights.
+//
+//   out[m, n] = round(inv_rms[m] * scale[n] * sum_k x[m,k] * q[n,k] + b[n])
+//
+// q is the gamma-folded weight quantized per output channel (symmetric,
+// scale[n] = max|W_fused[n,:]| / 127, q = clamp(round(W_fused / scale), +-127);
+// the quantizer of the reference's quantization-aware benchmark,
+// src/benchmark_kimi26_quantized.py:30-35).  Where the reference dequantizes
+// the whole weight to bf16 in HBM on every call and then runs F.linear on
+// x * bf16(inv_rms) (:38-39, :102-106), this kernel streams the int8 bytes
+// (half the weight traffic of bf16) and widens them to bf16 in shared memory
+// right before the tensor cores read them.  |q| <= 127 is exact in bf16, so
+// the product is the exact integer dot product accumulated in fp32; inv_rms
+// and scale are applied once, to the fp32 accumulator.
+//
+// Layout: the SM-pair (cta_group::2) kernel of frn_fused_linear_pair.cu with
+// one more role.  Per stage and CTA: x tile [128 x 64] bf16 (TMA, completes on
+// the even CTA's `full`), int8 W half-tile [BN/2 x 64] (TMA, 64B-swizzled,
+// completes on this CTA's `qfull`), and the bf16 copy of that half-tile that
+// the converter warps write in the UMMA 128B-swizzled K-major layout and then
+// announce on the even CTA's `conv` barrier (8 arrivals: 4 warps x 2 CTAs).
+//
+// Roles (each CTA): warps 0-3 epilogue, warps 4-5 producers (x and int8 W of
+// even / odd stages), warp 6 MMA (even CTA) + TMEM owner, warps 7-10 RMS,
+// warps 11-14 converters (thread = W row of the half-tile).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "frn_internal.h"
+#include "frn_ptx.cuh"
+
+namespace frn {
+
+struct W8Params {
+  int32_t M, N, K;
+  int32_t num_m_blocks, num_n_blocks, num_k_blocks;
+  float eps;
+  const float* scale;  // [N] per-output-channel dequantization scales
+  const void* bias;    // may be null
+  void* out;
+  int64_t out_row_stride;
+  uint64_t timeout_ns;
+};
+
+template <int BN, int STAGES>
+struct W8Cfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int BN_HALF = BN / 2;
+  static constexpr int A_BYTES = BM * BK * 2;        // bf16 x tile
+  static constexpr int Q_BYTES = BN_HALF * BK;        // int8 W half-tile
+  static constexpr int B_BYTES = BN_HALF * BK * 2;   // its bf16 copy
+  static constexpr uint32_t PAIR_A_TX = 2u * A_BYTES;
+  static constexpr uint32_t TMEM_COLS = (2 * BN <= 256) ? 256u : 512u;
+  static constexpr int STG_BYTES = 32 * 128;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_Q = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_STG = OFF_Q + STAGES * Q_BYTES;
+  static constexpr int OFF_RMS = OFF_STG + 4 * 2 * STG_BYTES;
+  static constexpr int OFF_BAR = OFF_RMS + 2 * BM * 4;
+  static constexpr int NUM_BARS = 5 * STAGES + 9;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static constexpr int EPI_WARPS = 4, RMS_WARPS = 4, CONV_WARPS = 4;
+  static constexpr int WARP_PROD0 = 4, WARP_MMA = 6, WARP_RMS0 = 7, WARP_CONV0 = 11;
+  static constexpr int THREADS = 32 * 15;
+  static_assert(BN_HALF <= 32 * CONV_WARPS, "one converter thread per W row");
+  static_assert(STAGES % 2 == 0, "stages are split between two producers");
+  static_assert(B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "stage buffers must stay aligned");
+  static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
+};
+
+// Four signed int8 (one 32-bit word) -> four exact fp32 values, without the
+// int->float converter: place the byte (biased by 128) in the low mantissa
+// bits of 2^23 and subtract 2^23 + 128 (the magic-number conversion used for
+// low-bit weight dequantization, e.g. Kim et al. 2022, "Who Says Elephants
+// Can't Run").
+__device__ __forceinline__ void s8x4_to_f32x4(uint32_t w, float (&f)[4]) {
+  const uint32_t u = w ^ 0x80808080u;  // q + 128 in every byte
+  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::THREADS, 1)
+    fused_rmsnorm_linear_w8_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                   const __grid_constant__ CUtensorMap tmap_q,
+                                   const W8Params p) {
+  using C = W8Cfg<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);  // even CTA: x of both CTAs
+  uint64_t* qfull = full + STAGES;                                 // this CTA's int8 tile
+  uint64_t* conv = qfull + STAGES;                                 // even CTA: bf16 W ready
+  uint64_t* mma_done = conv + STAGES;
+  uint64_t* empty = mma_done + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* rms_full = tmem_empty + 2;
+  uint64_t* rms_empty = rms_full + 2;
+  uint64_t* drain = rms_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+  float* rms_buf = reinterpret_cast<float*>(smem + C::OFF_RMS);
+
+  const uint32_t warp = warp_id_in_cta();
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t rank = cluster_cta_rank();
+  const uint32_t pair = blockIdx.x >> 1;
+  const uint32_t num_pairs = gridDim.x >> 1;
+
+  if (warp == C::WARP_PROD0 && lane == 0) {
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_q);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&qfull[s], 1);
+      mbar_init(&conv[s], 2 * C::CONV_WARPS);
+      mbar_init(&mma_done[s], 1);
+      mbar_init(&empty[s], C::RMS_WARPS);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 2 * C::EPI_WARPS);
+      mbar_init(&rms_full[a], C::RMS_WARPS);
+      mbar_init(&rms_empty[a], C::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_mbarrier_init();
+  }
+  if (warp == C::WARP_MMA) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  const int nkb = p.num_k_blocks;
+  const uint64_t to = p.timeout_ns;
+
+  if (warp == C::WARP_PROD0 || warp == C::WARP_PROD0 + 1) {
+    // Producer p issues the x tile and the int8 W half-tile of the stages
+    // with s % 2 == p.
+    if (lane == 0) {
+      griddep_wait();
+      const uint32_t parity_sel = warp - C::WARP_PROD0;
+      uint32_t stage = 0, phase = 0;
+      for (int t = pair; t < num_tiles; t += num_pairs) {
+        const int m0 = (t % p.num_m_blocks) * 2 * C::BM + rank * C::BM;
+        const int n0 = (t / p.num_m_blocks) * BN + rank * C::BN_HALF;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if ((stage & 1u) == parity_sel) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, to)) { ok = false; break; }
+            const uint32_t leader_full = mapa_shared(smem_addr(&full[stage]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], C::PAIR_A_TX);
+            tma_load_2d_pair(smem + C::OFF_A + stage * C::A_BYTES, &tmap_x, leader_full,
+                             kb * C::BK, m0);
+            mbar_arrive_expect_tx(&qfull[stage], C::Q_BYTES);
+            tma_load_2d(smem + C::OFF_Q + stage * C::Q_BYTES, &tmap_q, &qfull[stage], kb * C::BK,
+                        n0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == C::WARP_MMA) {
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = make_idesc_f16(Elem16<T>::kUmmaFormat, 2 * C::BM, BN);
+      uint32_t stage = 0, phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+        const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
+          if (!mbar_wait_cluster(&conv[stage], phase, abort_flag, to)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(smem + C::OFF_A + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / 16; ++k)
+            umma_f16_ss_pair(d_tmem, make_smem_desc_k_sw128(a_addr + k * 32),
+                             make_smem_desc_k_sw128(b_addr + k * 32), idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_mc(&mma_done[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&tmem_full[acc], 0x3);
+      }
+      umma_commit_pair_mc(drain, 0x1);
+      uint32_t zero = 0;
+      mbar_wait(drain, 0, &zero, to);
+    }
+  } else if (warp >= C::WARP_CONV0) {
+    // Converter thread j widens row j of this CTA's int8 half-tile.
+    const int j = static_cast<int>(threadIdx.x) - C::WARP_CONV0 * 32;
+    const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
+        if (j < C::BN_HALF) {
+          // int8 row j: 64 bytes, 64B-swizzled (16-byte chunk c at c ^ ((j >> 1) & 3)).
+          const uint8_t* qrow = smem + C::OFF_Q + stage * C::Q_BYTES + j * 64;
+          uint8_t* brow = smem + C::OFF_B + stage * C::B_BYTES + j * 128;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 w = *reinterpret_cast<const uint4*>(qrow + ((c ^ ((j >> 1) & 3)) << 4));
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // 8 int8 -> one 16-byte bf16 chunk
+              float f[8];
+              s8x4_to_f32x4(ws[2 * h], *reinterpret_cast<float(*)[4]>(&f[0]));
+              s8x4_to_f32x4(ws[2 * h + 1], *reinterpret_cast<float(*)[4]>(&f[4]));
+              uint4 o;
+              o.x = float2_to_pair<T>(f[0], f[1]);
+              o.y = float2_to_pair<T>(f[2], f[3]);
+              o.z = float2_to_pair<T>(f[4], f[5]);
+              o.w = float2_to_pair<T>(f[6], f[7]);
+              const int chunk = c * 2 + h;  // 16-byte chunk of the bf16 row
+              *reinterpret_cast<uint4*>(brow + ((chunk ^ (j & 7)) << 4)) = o;
+            }
+          }
+        }
+        // The tensor cores (async proxy) read what was just written.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(leader_conv0 + stage * 8);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp >= C::WARP_RMS0) {
+    const int r = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;
+    const float inv_k = 1.0f / static_cast<float>(p.K);
+    uint32_t stage = 0, phase = 0;
+    int gen = -1, cur_m = -1;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+      const int mb = t % p.num_m_blocks;
+      const bool first = (mb != cur_m);
+      if (first) { ++gen; cur_m = mb; }
+      float ss0 = 0.f, ss1 = 0.f;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
+        if (first) {
+          const uint8_t* row = smem + C::OFF_A + stage * C::A_BYTES + r * 128;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (r & 7)) << 4));
+            const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
+            const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
+            ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
+            ss0 = fmaf(f1.x, f1.x, ss0); ss1 = fmaf(f1.y, f1.y, ss1);
+            ss0 = fmaf(f2.x, f2.x, ss0); ss1 = fmaf(f2.y, f2.y, ss1);
+            ss0 = fmaf(f3.x, f3.x, ss0); ss1 = fmaf(f3.y, f3.y, ss1);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (!ok || !first) continue;
+      const uint32_t g = static_cast<uint32_t>(gen);
+      if (!mbar_wait(&rms_empty[g & 1], ((g >> 1) & 1) ^ 1u, abort_flag, to)) break;
+      rms_buf[(g & 1) * C::BM + r] = rsqrtf((ss0 + ss1) * inv_k + p.eps);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rms_full[g & 1]);
+    }
+  } else {
+    // Epilogue warps 0-3 (same as the bf16 pair kernel, plus scale[n]).
+    const uint32_t q = warp;
+    const bool has_bias = p.bias != nullptr;
+    const uint4* bias16 = reinterpret_cast<const uint4*>(p.bias);
+    const float4* scale4 = reinterpret_cast<const float4*>(p.scale);
+    const uint32_t leader_tmem_empty0 = mapa_shared(smem_addr(&tmem_empty[0]), 0);
+    griddep_wait();
+    int i = 0;
+    int gen = -1, cur_m = -1;
+    float inv_rms = 0.f;
+    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
+      const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+      const int mb = t % p.num_m_blocks;
+      const int row_base = mb * 2 * C::BM + rank * C::BM + q * 32;
+      const int n0 = (t / p.num_m_blocks) * BN;
+      const bool first = (mb != cur_m);
+      const bool last = (t + static_cast<int>(num_pairs) >= num_tiles) ||
+                        ((t + static_cast<int>(num_pairs)) % p.num_m_blocks != mb);
+      if (first) { ++gen; cur_m = mb; }
+      const uint32_t g = static_cast<uint32_t>(gen);
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) break;
+      if (first) {
+        if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) break;
+        inv_rms = rms_buf[(g & 1) * C::BM + q * 32 + lane];
+      }
+      tc_fence_after();
+      if (last) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
+      }
+      const uint32_t taddr = tmem_base + acc * BN + ((q * 32u) << 16);
+      constexpr int NCHUNK = BN / 64 + (BN % 64 ? 1 : 0);
+#pragma unroll 1
+      for (int c = 0; c < NCHUNK; ++c) {
+        const bool half = (c * 64 + 32 >= BN);
+        uint32_t v[64];
+        tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_wait();
+        if (c == NCHUNK - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
+        }
+        uint8_t* sb = smem + C::OFF_STG + (q * 2 + (c & 1)) * C::STG_BYTES;
+        const int col0 = n0 + c * 64;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          if (half && jj >= 4) break;
+          const int col = col0 + jj * 8;
+          float f[8];
+          float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+          if (col < p.N) {
+            s0 = __ldg(scale4 + col / 4);
+            s1 = __ldg(scale4 + col / 4 + 1);
+          }
+          const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[jj * 8 + e]) * inv_rms * sc[e];
+          if (has_bias && col < p.N) {
+            const uint4 bv = __ldg(bias16 + col / 8);
+            const float2 b0 = pair_to_float2<T>(bv.x), b1 = pair_to_float2<T>(bv.y);
+            const float2 b2 = pair_to_float2<T>(bv.z), b3 = pair_to_float2<T>(bv.w);
+            f[0] += b0.x; f[1] += b0.y; f[2] += b1.x; f[3] += b1.y;
+            f[4] += b2.x; f[5] += b2.y; f[6] += b3.x; f[7] += b3.y;
+          }
+          uint4 o;
+          o.x = float2_to_pair<T>(f[0], f[1]);
+          o.y = float2_to_pair<T>(f[2], f[3]);
+          o.z = float2_to_pair<T>(f[4], f[5]);
+          o.w = float2_to_pair<T>(f[6], f[7]);
+          *reinterpret_cast<uint4*>(sb + lane * 128 + ((jj ^ (lane & 7)) << 4)) = o;
+        }
+        __syncwarp();
+        const int chunk = static_cast<int>(lane & 7);
+        const int col = col0 + chunk * 8;
+        const bool col_ok = col < p.N && !(half && chunk >= 4);
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+          const int r = ii * 4 + static_cast<int>(lane >> 3);
+          const uint4 o = *reinterpret_cast<const uint4*>(sb + r * 128 + ((chunk ^ (r & 7)) << 4));
+          const int grow = row_base + r;
+          if (col_ok && grow < p.M)
+            st_global_v4(static_cast<T*>(p.out) + static_cast<int64_t>(grow) * p.out_row_stride + col,
+                         o.x, o.y, o.z, o.w);
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();
+  if (*abort_flag) __nanosleep(20000);
+  if (warp == C::WARP_MMA) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ quantizer
+
+// Symmetric per-output-channel int8 quantization of the folded weight, one CTA
+// per row: scale = max(|w|, 1e-8) / 127 in fp32, q = clamp(rint(w / scale),
+// -127, 127) -- round half to even, IEEE division, exactly torch.round(w /
+// scale).clamp(-127, 127) of the reference (src/benchmark_kimi26_quantized.py:30-35).
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const T* __restrict__ w, int64_t ws,
+                                                            int K, int8_t* __restrict__ q,
+                                                            int64_t qs, float* __restrict__ scale) {
+  __shared__ float red[8];
+  const T* row = w + static_cast<int64_t>(blockIdx.x) * ws;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += 256) amax = fmaxf(amax, fabsf(static_cast<float>(row[k])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+  const float sc = fmaxf(m, 1e-8f) / 127.0f;
+  if (threadIdx.x == 0) scale[blockIdx.x] = sc;
+  int8_t* qrow = q + static_cast<int64_t>(blockIdx.x) * qs;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    float v = rintf(static_cast<float>(row[k]) / sc);
+    v = fminf(fmaxf(v, -127.f), 127.f);
+    qrow[k] = static_cast<int8_t>(v);
+  }
+}
+
+int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws, void* q,
+                      int64_t qs, float* scale, cudaStream_t s) {
+  if (dtype == FRN_DTYPE_BF16)
+    quantize_rows_kernel<__nv_bfloat16><<<static_cast<unsigned>(N), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(w), ws, static_cast<int>(K), static_cast<int8_t*>(q), qs,
+        scale);
+  else if (dtype == FRN_DTYPE_F16)
+    quantize_rows_kernel<__half><<<static_cast<unsigned>(N), 256, 0, s>>>(
+        static_cast<const __half*>(w), ws, static_cast<int>(K), static_cast<int8_t*>(q), qs, scale);
+  else if (dtype == FRN_DTYPE_F32)
+    quantize_rows_kernel<float><<<static_cast<unsigned>(N), 256, 0, s>>>(
+        static_cast<const float*>(w), ws, static_cast<int>(K), static_cast<int8_t*>(q), qs, scale);
+  else
+    return set_error(FRN_ERR_UNSUPPORTED, "quantize: weight dtype must be fp32, fp16 or bf16");
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("launch quantize_rows", e);
+  return 0;
+}
+
+// ------------------------------------------------------------------ host side
+
+template <typename T, int BN, int STAGES>
+static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
+  using C = W8Cfg<BN, STAGES>;
+  auto kern = fused_rmsnorm_linear_w8_kernel<T, BN, STAGES>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  static int max_pairs[kMaxDevices] = {};
+  if (dev < kMaxDevices && max_pairs[dev] == 0) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(w8 kernel)", e);
+    cudaLaunchConfig_t qc = {};
+    qc.gridDim = dim3(2 * 74);
+    qc.blockDim = dim3(C::THREADS);
+    qc.dynamicSmemBytes = C::SMEM_BYTES;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = 2;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    qc.attrs = qa;
+    qc.numAttrs = 1;
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &qc);
+    if (e != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = sm_count(dev) / 2;
+    }
+    max_pairs[dev] = clusters;
+  }
+  const int pairs_avail = dev < kMaxDevices ? max_pairs[dev] : sm_count(dev) / 2;
+  const CUtensorMapDataType dt = Elem16<T>::kTmaType;
+  CUtensorMap tx, tq;
+  int rc = encode_tmap_2d(&tx, dt, 2, pr.x, pr.K, pr.M, pr.x_row_stride, C::BK, C::BM,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_tmap_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, pr.wq, pr.K, pr.N, pr.wq_row_stride,
+                      C::BK, C::BN_HALF, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  W8Params p;
+  p.M = static_cast<int32_t>(pr.M);
+  p.N = static_cast<int32_t>(pr.N);
+  p.K = static_cast<int32_t>(pr.K);
+  p.num_m_blocks = static_cast<int32_t>((pr.M + 2 * C::BM - 1) / (2 * C::BM));
+  p.num_n_blocks = static_cast<int32_t>((pr.N + BN - 1) / BN);
+  p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
+  p.eps = pr.eps;
+  p.scale = pr.scale;
+  p.bias = pr.bias;
+  p.out = pr.out;
+  p.out_row_stride = pr.out_row_stride;
+  p.timeout_ns = wait_timeout_ns();
+  const int tiles = p.num_m_blocks * p.num_n_blocks;
+  const int pairs = tiles < pairs_avail ? tiles : pairs_avail;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tq, p);
+  if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_w8", e);
+  return 0;
+}
+
+template <typename T>
+static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
+  const int bn = choose_pair_kernel(pr.M, pr.N, sm_count(0) / 2);
+  switch (bn) {
+    case 256: return launch_w8<T, 256, 4>(pr, s);
+    case 224: return launch_w8<T, 224, 4>(pr, s);
+    case 192: return launch_w8<T, 192, 4>(pr, s);
+    case 160: return launch_w8<T, 160, 4>(pr, s);
+    default: return launch_w8<T, 128, 4>(pr, s);
+  }
+}
+
+int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s) {
+  if (pr.dtype == FRN_DTYPE_BF16) return run_w8_t<__nv_bfloat16>(pr, s);
+  if (pr.dtype == FRN_DTYPE_F16) return run_w8_t<__half>(pr, s);
+  return set_error(FRN_ERR_UNSUPPORTED, "int8-weight RMSNorm+Linear takes bf16 or fp16 x");
+}
+
+}  // namespace frn

@@ -30,6 +30,20 @@ struct LinearProblem {
   size_t workspace_bytes;
 };
 
+// One int8-weight problem (strides in elements; wq_row_stride in bytes).
+struct W8Problem {
+  int dtype;
+  const void* x;
+  int64_t M, K, x_row_stride;
+  const int8_t* wq;
+  int64_t N, wq_row_stride;
+  const float* scale;
+  const void* bias;
+  float eps;
+  void* out;
+  int64_t out_row_stride;
+};
+
 // Records `msg` as this thread's last error and returns `code`.
 int set_error(int code, const char* fmt, ...);
 // Records a CUDA failure ("<what>: <cuda error string>") and returns FRN_ERR_CUDA.
@@ -54,6 +68,10 @@ int run_fused_linear_pair(const LinearProblem& pr, int bn, cudaStream_t s);
 // Decode (M <= 128) swap-AB kernel, `split` CTAs per cluster along K.
 int choose_decode_split(int64_t N, int64_t K, int sms);
 int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s);
+
+int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s);
+int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws, void* q,
+                      int64_t qs, float* scale, cudaStream_t s);
 
 int run_rmsnorm_normalize(int dtype, const void* x, int64_t xs, void* out, int64_t os,
                           const void* b, int64_t rows, int64_t h, int64_t n, float eps,

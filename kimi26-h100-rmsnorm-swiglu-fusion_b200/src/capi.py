@@ -57,6 +57,15 @@ PROTOTYPES = {
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
          c_float, c_void_p, c_int64, c_void_p, c_size_t, c_int, c_void_p],
     ),
+    "frn_fused_rmsnorm_linear_w8": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+         c_void_p, c_float, c_void_p, c_int64, c_void_p],
+    ),
+    "frn_quantize_int8_per_channel": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
+    ),
     "frn_device_error": (c_int, [c_int, ctypes.POINTER(c_uint32), c_int]),
 }
 
@@ -143,6 +152,37 @@ def rmsnorm_normalize(x, raw_output, b_new, h: int, eps: float, threads: int = 2
         _stream_ptr(x.device))
     check(rc, "frn_rmsnorm_normalize")
     return raw_output
+
+
+def fused_rmsnorm_linear_w8(x, wq, w_scale, bias=None, eps: float = 1e-6, out=None):
+    """out = inv_rms[:,None] * w_scale[None,:] * (x @ wq.T) + bias (int8 wq)."""
+    import torch
+
+    assert x.dim() == 2 and wq.dim() == 2 and x.stride(1) == 1 and wq.stride(1) == 1
+    M, K = x.shape
+    N = wq.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    rc = lib().frn_fused_rmsnorm_linear_w8(
+        _dtype_code(x), x.data_ptr(), M, K, x.stride(0), wq.data_ptr(), N, wq.stride(0),
+        w_scale.data_ptr(), bias.data_ptr() if bias is not None else None, float(eps),
+        out.data_ptr(), out.stride(0), _stream_ptr(x.device))
+    check(rc, "frn_fused_rmsnorm_linear_w8")
+    return out
+
+
+def quantize_int8_per_channel(w):
+    """(q int8 [N,K], scale fp32 [N]) of a weight on the GPU."""
+    import torch
+
+    N, K = w.shape
+    q = torch.empty(N, K, dtype=torch.int8, device=w.device)
+    scale = torch.empty(N, dtype=torch.float32, device=w.device)
+    rc = lib().frn_quantize_int8_per_channel(_dtype_code(w), w.data_ptr(), N, K, w.stride(0),
+                                             q.data_ptr(), K, scale.data_ptr(),
+                                             _stream_ptr(w.device))
+    check(rc, "frn_quantize_int8_per_channel")
+    return q, scale
 
 
 def device_error(device: int = 0, clear: bool = False) -> int:

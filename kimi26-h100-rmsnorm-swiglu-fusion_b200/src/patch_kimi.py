@@ -22,11 +22,15 @@ import torch
 import torch.nn as nn
 
 from src.fused_forward import FusedRMSNormLinearV1, FusedRMSNormLinearV3
+from src.quantized import FusedRMSNormLinearInt8
 from src.weight_transform import compute_fused_weights_rmsnorm
 
+# "V1"/"V3" as in the reference; "INT8" quantizes the folded weight per output
+# channel and runs the int8-weight fused kernel.
 _VARIANT_CLASSES = {
     "V1": FusedRMSNormLinearV1,
     "V3": FusedRMSNormLinearV3,
+    "INT8": FusedRMSNormLinearInt8,
 }
 
 # (norm attribute, linear attribute, count key) of the pairs this patch fuses.
@@ -89,7 +93,8 @@ def patch_kimi_q_lora_norms(model, device=None, variant: str = "V3") -> dict[str
         model: Kimi K2.6 (DeepseekV3-style) HF model or its text model.
         device: where the fused weights live; default: the model's first
             parameter's device.
-        variant: "V1" or "V3" (both run the same sm_100a fused kernel).
+        variant: "V1" or "V3" (both run the same sm_100a fused kernel), or
+            "INT8" for int8 per-channel weights.
 
     Returns:
         ``{"q_a_layernorm_to_q_b_proj": n_q, "kv_a_layernorm_to_kv_b_proj": n_kv}``.
