@@ -1,0 +1,174 @@
+"""Multi-GPU launchers for fused RMSNorm -> Linear (one box, NVLink/NVSwitch).
+
+The reference is single-GPU.  Rows (tokens) of this op are independent --
+inv_rms is per row and the GEMM is row-separable -- so large-M work is split
+token-wise across GPUs with the weight replicated and NO collective on the
+data path.  For weight-bound (decode) shapes the weight itself can instead be
+split by output columns, with an NCCL all-gather only when a consumer needs
+the full row.
+
+Two flavours of the token split:
+
+* ``TokenPartitionedFusedLinear`` -- one process driving several devices:
+  the weight is replicated once per device, each call slices x into
+  contiguous row shards, launches every shard on its own device's current
+  stream (asynchronously) and either returns the per-device outputs or
+  copies them into one tensor on a destination device.
+* ``fused_rmsnorm_linear_token_parallel`` -- one process per GPU under
+  torch.distributed: every rank runs its own shard; ``gather=True`` adds an
+  all-gather (for consumers that need every row on every rank).
+
+``ColumnParallelFusedLinear`` holds W[N-slice] per rank and all-gathers the
+[M, N/world] outputs into [M, N] over NCCL.
+
+The per-shard op is ``denominator_cuda.fused_rmsnorm_linear`` by default; it
+can be replaced (``op=``) so the partition / gather logic can be exercised on
+CPU ranks with the gloo backend.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Optional, Sequence
+
+import torch
+
+FusedOp = Callable[[torch.Tensor, torch.Tensor, Optional[torch.Tensor], float], torch.Tensor]
+
+
+def _default_op() -> FusedOp:
+    from src.load_cuda import denominator_cuda
+
+    return lambda x, w, b, eps: denominator_cuda.fused_rmsnorm_linear(x, w, b, float(eps))
+
+
+def shard_bounds(total: int, parts: int, index: int) -> tuple[int, int]:
+    """[start, end) of contiguous shard `index` of `total` rows over `parts`;
+    the first (total % parts) shards take one extra row."""
+    if parts <= 0 or not 0 <= index < parts:
+        raise ValueError(f"bad shard {index} of {parts}")
+    base, rem = divmod(total, parts)
+    start = index * base + min(index, rem)
+    return start, start + base + (1 if index < rem else 0)
+
+
+def column_bounds(n: int, parts: int, index: int, align: int = 8) -> tuple[int, int]:
+    """Column slice of rank `index` for a column split of width n, in units of
+    `align` columns (16-byte rows for the fused kernel); n % align == 0."""
+    if n % align:
+        raise ValueError(f"N={n} is not a multiple of {align}")
+    s, e = shard_bounds(n // align, parts, index)
+    return s * align, e * align
+
+
+class TokenPartitionedFusedLinear:
+    """Fused RMSNorm -> Linear over several GPUs of one process, split by rows.
+
+    W_new / b_new are replicated to every device in `devices` at construction.
+    ``__call__(x)`` returns a list of per-device outputs (rows in order) or,
+    with ``out_device``, one [M, N] tensor gathered there.  Work on each device
+    is enqueued on that device's current stream; the host does not wait.
+    """
+
+    def __init__(self, W_new: torch.Tensor, b_new: Optional[torch.Tensor], eps: float,
+                 devices: Sequence[torch.device | str | int], op: Optional[FusedOp] = None):
+        self.devices = [torch.device(d) if not isinstance(d, int) else torch.device("cuda", d)
+                        for d in devices]
+        if not self.devices:
+            raise ValueError("need at least one device")
+        self.eps = float(eps)
+        self.weights = [W_new.to(d) for d in self.devices]
+        self.biases = [b_new.to(d) if b_new is not None else None for d in self.devices]
+        self.op = op or _default_op()
+
+    def shards(self, m: int) -> list[tuple[int, int]]:
+        return [shard_bounds(m, len(self.devices), i) for i in range(len(self.devices))]
+
+    def __call__(self, x: torch.Tensor, out_device=None):
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        outs = []
+        for (s, e), dev, w, b in zip(self.shards(x2.shape[0]), self.devices, self.weights,
+                                     self.biases):
+            xs = x2[s:e]
+            if xs.device != dev:
+                xs = xs.to(dev, non_blocking=True)
+            outs.append(self.op(xs, w, b, self.eps) if e > s else
+                        torch.empty(0, w.shape[0], dtype=x.dtype, device=dev))
+        if out_device is None:
+            return outs
+        dst = torch.device(out_device)
+        full = torch.empty(x2.shape[0], self.weights[0].shape[0], dtype=x.dtype, device=dst)
+        for (s, e), o in zip(self.shards(x2.shape[0]), outs):
+            if e > s:
+                full[s:e].copy_(o, non_blocking=True)
+        return full.reshape(*lead, full.shape[-1])
+
+
+def fused_rmsnorm_linear_token_parallel(x_local: torch.Tensor, W_new: torch.Tensor,
+                                        b_new: Optional[torch.Tensor], eps: float, *,
+                                        gather: bool = False, group=None,
+                                        op: Optional[FusedOp] = None) -> torch.Tensor:
+    """One rank's share of a token-partitioned fused RMSNorm -> Linear.
+
+    x_local holds this rank's rows; W_new is the rank's replica.  With
+    ``gather=False`` (the default) no communication happens.  With
+    ``gather=True`` the [M_local, N] outputs of all ranks are all-gathered
+    (ranks may hold different row counts) and returned as [sum M, N] in rank
+    order."""
+    import torch.distributed as dist
+
+    op = op or _default_op()
+    out = op(x_local, W_new, b_new, eps)
+    if not gather:
+        return out
+    world = dist.get_world_size(group)
+    counts = torch.tensor([out.shape[0]], dtype=torch.int64, device=out.device)
+    all_counts = [torch.zeros_like(counts) for _ in range(world)]
+    dist.all_gather(all_counts, counts, group=group)
+    sizes = [int(c.item()) for c in all_counts]
+    mx = max(sizes)
+    padded = out.new_zeros(mx, out.shape[1])
+    padded[: out.shape[0]] = out
+    bufs = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(bufs, padded, group=group)
+    return torch.cat([b[:n] for b, n in zip(bufs, sizes)], dim=0)
+
+
+class ColumnParallelFusedLinear:
+    """Column (N) split: this rank holds W[cols] and produces out[:, cols].
+
+    ``__call__(x, gather=True)`` all-gathers the [M, N/world] slices of every
+    rank and returns [M, N]; the gather runs over NCCL (NVLink) on GPUs.  Kimi
+    kv_b's N = 64 heads x 256, so rank slices can be head-aligned by choosing
+    ``align`` = one head's width.
+    """
+
+    def __init__(self, W_full: torch.Tensor, b_full: Optional[torch.Tensor], eps: float, *,
+                 rank: int, world: int, group=None, align: int = 8,
+                 op: Optional[FusedOp] = None, device=None):
+        self.n = W_full.shape[0]
+        self.rank, self.world, self.group = rank, world, group
+        self.bounds = [column_bounds(self.n, world, r, align) for r in range(world)]
+        s, e = self.bounds[rank]
+        dev = device if device is not None else W_full.device
+        self.w = W_full[s:e].contiguous().to(dev)
+        self.b = b_full[s:e].contiguous().to(dev) if b_full is not None else None
+        self.eps = float(eps)
+        self.op = op or _default_op()
+
+    def __call__(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        import torch.distributed as dist
+
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        part = self.op(x2, self.w, self.b, self.eps)
+        if not gather:
+            return part.reshape(*lead, part.shape[-1])
+        widths = [e - s for s, e in self.bounds]
+        mx = max(widths)
+        padded = part.new_zeros(x2.shape[0], mx)
+        padded[:, : part.shape[1]] = part
+        bufs = [torch.empty_like(padded) for _ in range(self.world)]
+        dist.all_gather(bufs, padded, group=self.group)
+        full = torch.cat([b[:, :w] for b, w in zip(bufs, widths)], dim=1)
+        return full.reshape(*lead, self.n)

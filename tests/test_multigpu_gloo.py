@@ -1,0 +1,97 @@
+"""Host logic of the multi-GPU launchers on CPU: shard arithmetic, and the
+token-parallel and column-parallel paths as world_size-2 gloo process groups
+with the oracle's fp32 math standing in for the CUDA op."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import rmsnorm_linear as orc
+from src import multigpu
+
+
+def _cpu_op(x, w, b, eps):
+    return orc.fp32_truth(x, w, b, eps)
+
+
+def test_shard_bounds_cover_exactly():
+    for total in (0, 1, 5, 512, 4097):
+        for parts in (1, 2, 3, 8):
+            bounds = [multigpu.shard_bounds(total, parts, i) for i in range(parts)]
+            assert bounds[0][0] == 0 and bounds[-1][1] == total
+            assert all(b[1] == c[0] for b, c in zip(bounds, bounds[1:]))
+            sizes = [e - s for s, e in bounds]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        multigpu.shard_bounds(10, 2, 2)
+
+
+def test_column_bounds_aligned():
+    b = [multigpu.column_bounds(16384, 8, r, align=256) for r in range(8)]
+    assert b[0] == (0, 2048) and b[-1] == (14336, 16384)
+    with pytest.raises(ValueError):
+        multigpu.column_bounds(100, 2, 0)
+
+
+def test_single_process_token_partition_on_cpu_devices():
+    x, gamma, W = orc.make_inputs(37, 64, 24, seed=1, dtype=torch.float32)
+    Wn = orc.fold_gamma(W, gamma)
+    tp = multigpu.TokenPartitionedFusedLinear(Wn, None, orc.EPS, ["cpu", "cpu", "cpu"],
+                                              op=_cpu_op)
+    parts = tp(x)
+    assert [p.shape[0] for p in parts] == [13, 12, 12]
+    full = tp(x.view(1, 37, 64), out_device="cpu")
+    torch.testing.assert_close(full.view(37, 24), _cpu_op(x, Wn, None, orc.EPS))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        M, K, N = 45, 32, 48
+        x, gamma, W = orc.make_inputs(M, K, N, seed=3, dtype=torch.float32)
+        Wn = orc.fold_gamma(W, gamma)
+        b = torch.linspace(-1, 1, N)
+        s, e = multigpu.shard_bounds(M, world, rank)
+        local = multigpu.fused_rmsnorm_linear_token_parallel(x[s:e], Wn, b, orc.EPS, op=_cpu_op)
+        gathered = multigpu.fused_rmsnorm_linear_token_parallel(x[s:e], Wn, b, orc.EPS,
+                                                                gather=True, op=_cpu_op)
+        col = multigpu.ColumnParallelFusedLinear(Wn, b, orc.EPS, rank=rank, world=world,
+                                                 align=8, op=_cpu_op)
+        colfull = col(x.view(5, 9, K))
+        want = _cpu_op(x, Wn, b, orc.EPS)
+        results[rank] = (
+            torch.allclose(local, want[s:e], atol=1e-5),
+            torch.allclose(gathered, want, atol=1e-5),
+            torch.allclose(colfull.view(M, N), want, atol=1e-5),
+        )
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_gloo_world2_token_and_column_parallel():
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+        assert p.exitcode == 0
+    assert dict(results) == {0: (True, True, True), 1: (True, True, True)}
