@@ -144,6 +144,10 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Let the next kernel in the stream get scheduled now: its CTAs take SMs as
+  // ours retire and run their set-up while we finish; its griddepcontrol.wait
+  // still orders all of its global accesses after this whole grid.
+  griddep_launch_dependents();
 
   if (warp >= C::WARP_PROD0 && warp < C::WARP_PROD0 + 4) {
     // Four issuing threads (a single thread keeps only a few bulk-tensor

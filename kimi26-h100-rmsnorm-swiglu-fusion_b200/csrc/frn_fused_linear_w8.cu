@@ -148,6 +148,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
   const int num_tiles = p.num_m_blocks * p.num_n_blocks;
   const int nkb = p.num_k_blocks;
   const uint64_t to = p.timeout_ns;
+  // Let the next kernel in the stream get scheduled now: its CTAs take SMs as
+  // ours retire and run their set-up while we finish; its griddepcontrol.wait
+  // still orders all of its global accesses after this whole grid.
+  griddep_launch_dependents();
 
   if (warp == C::WARP_PROD0 || warp == C::WARP_PROD0 + 1) {
     // Producer p issues the x tile and the int8 W half-tile of the stages
