@@ -397,11 +397,13 @@ def run_ours(args):
         achieved, peak, unit = bytes_of(M, K, N) / per_launch_s / 1e9, hbm_gbs, "GB/s"
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
                 "frac": achieved / peak, "traffic": read_profiled_traffic(
-                    "fused_rmsnorm_linear", args.config),
+                    "fused_rmsnorm_linear" if M > 128 else "fused_rmsnorm_linear_decode",
+                    args.config),
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json burst figures)"
                 if peak_src == "measured" else "fallback",
                 "roofline_frac_of_max_time": roof_time / per_launch_s,
-                "kernel": "fused_rmsnorm_linear_kernel",
+                "kernel": ("fused_rmsnorm_linear_pair_kernel" if M > 128
+                           else "fused_rmsnorm_linear_decode_kernel"),
                 "algorithmic_bytes_per_launch": bytes_of(M, K, N),
                 "algorithmic_flops_per_launch": flops}
 
