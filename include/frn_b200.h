@@ -56,7 +56,11 @@ extern "C" {
 #define FRN_KERNEL_PAIR_N192    7  /* SM pair per 256x192 tile                */
 #define FRN_KERNEL_PAIR_N224    8  /* SM pair per 256x224 tile                */
 #define FRN_KERNEL_PAIR_N256    9  /* SM pair per 256x256 tile                */
-#define FRN_KERNEL_PAIR_AUTO   10  /* SM pair, tile width chosen by (M, N)    */
+#define FRN_KERNEL_PAIR_AUTO   10  /* SM pair, tiling chosen by (M, N, K)     */
+#define FRN_KERNEL_WIDE_N128   11  /* SM pair, two accumulators: 256x(2*128)  */
+#define FRN_KERNEL_WIDE_N192   12  /* SM pair, two accumulators: 256x(2*192)  */
+#define FRN_KERNEL_WIDE_N224   13  /* SM pair, two accumulators: 256x(2*224)  */
+#define FRN_KERNEL_WIDE_N256   14  /* SM pair, two accumulators: 256x(2*256)  */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */

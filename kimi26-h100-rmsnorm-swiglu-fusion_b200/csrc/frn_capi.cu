@@ -182,12 +182,16 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
   const int sms = sm_count(dev);
   if (kernel == FRN_KERNEL_AUTO) kernel = (M <= 128) ? FRN_KERNEL_DECODE : FRN_KERNEL_PAIR_AUTO;
   if (kernel == FRN_KERNEL_PAIR_AUTO)
-    return run_fused_linear_pair(p, choose_pair_kernel(M, N, sms / 2), s);
+    return run_fused_linear_pair(p, choose_pair_tiling(M, N, K, sms / 2), s);
   if (kernel >= FRN_KERNEL_TILE_N128 && kernel <= FRN_KERNEL_TILE_N256)
     return run_fused_linear_prefill(p, kernel, s);
   if (kernel >= FRN_KERNEL_PAIR_N128 && kernel <= FRN_KERNEL_PAIR_N256) {
     static const int bns[5] = {128, 160, 192, 224, 256};
-    return run_fused_linear_pair(p, bns[kernel - FRN_KERNEL_PAIR_N128], s);
+    return run_fused_linear_pair(p, PairChoice{bns[kernel - FRN_KERNEL_PAIR_N128], 1}, s);
+  }
+  if (kernel >= FRN_KERNEL_WIDE_N128 && kernel <= FRN_KERNEL_WIDE_N256) {
+    static const int bns[4] = {128, 192, 224, 256};
+    return run_fused_linear_pair(p, PairChoice{bns[kernel - FRN_KERNEL_WIDE_N128], 2}, s);
   }
   if (kernel == FRN_KERNEL_DECODE) {
     if (M > 128)

@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 
 #include "frn_internal.h"
@@ -47,19 +48,25 @@ struct PairParams {
   uint64_t timeout_ns;
 };
 
-template <int BN, int STAGES>
+// NACC accumulators of BN columns per pair tile: NACC = 1 double-buffers the
+// accumulator in TMEM (tile i's epilogue overlaps tile i+1's mainloop); NACC
+// = 2 makes the tile 256 x 2*BN so one x tile feeds two W tiles (25% fewer
+// L2->SM bytes per MMA) and uses the TMEM columns for that instead.
+template <int BN, int STAGES, int NACC>
 struct PairCfg {
   static constexpr int BM = 128;  // rows per CTA
   static constexpr int BK = 64;
   static constexpr int BN_HALF = BN / 2;
+  static constexpr int TILE_N = NACC * BN;  // output columns per pair tile
+  static constexpr int NBUF = NACC == 1 ? 2 : 1;  // TMEM accumulator buffers
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN_HALF * BK * 2;
-  static constexpr uint32_t PAIR_TX = 2u * (A_BYTES + B_BYTES);
-  static constexpr uint32_t TMEM_COLS = (2 * BN <= 256) ? 256u : 512u;
+  static constexpr int B_BYTES = BN_HALF * BK * 2;  // one accumulator's W half-tile
+  static constexpr uint32_t PAIR_TX = 2u * (A_BYTES + NACC * B_BYTES);
+  static constexpr uint32_t TMEM_COLS = (NBUF * TILE_N <= 256) ? 256u : 512u;
   static constexpr int STG_BYTES = 32 * 128;  // one warp's 32 rows x 64 columns
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-  static constexpr int OFF_STG = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_STG = OFF_B + STAGES * NACC * B_BYTES;
   static constexpr int OFF_RMS = OFF_STG + 4 * 2 * STG_BYTES;
   static constexpr int OFF_BAR = OFF_RMS + 2 * BM * 4;
   static constexpr int NUM_BARS = 3 * STAGES + 9;
@@ -73,16 +80,18 @@ struct PairCfg {
   static constexpr int THREADS = 32 * (EPI_WARPS + 5 + RMS_WARPS);
   static_assert(STAGES % 2 == 0, "stages are split between two producers per operand");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(NACC == 1 || NACC == 2, "NACC");
+  static_assert(NBUF * TILE_N <= 512, "TMEM has 512 columns");
   static_assert(B_BYTES % 1024 == 0, "stage buffers must stay 1024-aligned");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
-template <typename T, int BN, int STAGES>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>::THREADS, 1)
+template <typename T, int BN, int STAGES, int NACC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, NACC>::THREADS, 1)
     fused_rmsnorm_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                      const __grid_constant__ CUtensorMap tmap_w,
                                      const PairParams p) {
-  using C = PairCfg<BN, STAGES>;
+  using C = PairCfg<BN, STAGES, NACC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -115,7 +124,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 2 * C::EPI_WARPS);
+      mbar_init(&tmem_empty[a], 2 * C::EPI_WARPS);  // only the first NBUF are used
       mbar_init(&rms_full[a], C::RMS_WARPS);
       mbar_init(&rms_empty[a], C::EPI_WARPS);
     }
@@ -153,7 +162,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
       uint32_t stage = 0, phase = 0;
       for (int t = pair; t < num_tiles; t += num_pairs) {
         const int m0 = (t % p.num_m_blocks) * 2 * C::BM + rank * C::BM;
-        const int n0 = (t / p.num_m_blocks) * BN + rank * C::BN_HALF;
+        const int n0 = (t / p.num_m_blocks) * C::TILE_N + rank * C::BN_HALF;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
           if ((stage & 1u) == parity_sel) {
@@ -164,8 +173,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
               tma_load_2d_pair(smem + C::OFF_A + stage * C::A_BYTES, &tmap_x, leader_full,
                                kb * C::BK, m0);
             else
-              tma_load_2d_pair(smem + C::OFF_B + stage * C::B_BYTES, &tmap_w, leader_full,
-                               kb * C::BK, n0);
+#pragma unroll
+              for (int j = 0; j < NACC; ++j)
+                tma_load_2d_pair(smem + C::OFF_B + (stage * NACC + j) * C::B_BYTES, &tmap_w,
+                                 leader_full, kb * C::BK, n0 + j * BN);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -179,20 +190,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
       int i = 0;
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
-        const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+        const uint32_t acc = i % C::NBUF, acc_phase = (i / C::NBUF) & 1;
         if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * C::TILE_N;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + C::OFF_A + stage * C::A_BYTES);
-          const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * C::B_BYTES);
+          const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * NACC * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < C::BK / 16; ++k) {
-            umma_f16_ss_pair(d_tmem, make_smem_desc_k_sw128(a_addr + k * 32),
-                             make_smem_desc_k_sw128(b_addr + k * 32), idesc,
-                             (kb > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+            for (int j = 0; j < NACC; ++j)
+              umma_f16_ss_pair(d_tmem + j * BN, make_smem_desc_k_sw128(a_addr + k * 32),
+                               make_smem_desc_k_sw128(b_addr + j * C::B_BYTES + k * 32), idesc,
+                               (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&mma_done[stage], 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -254,10 +267,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
     int gen = -1, cur_m = -1;
     float inv_rms = 0.f;
     for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
-      const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+      const uint32_t acc = i % C::NBUF, acc_phase = (i / C::NBUF) & 1;
       const int mb = t % p.num_m_blocks;
       const int row = mb * 2 * C::BM + rank * C::BM + q * 32 + lane;
-      const int n0 = (t / p.num_m_blocks) * BN;
+      const int n0 = (t / p.num_m_blocks) * C::TILE_N;
       const bool first = (mb != cur_m);
       const bool last = (t + static_cast<int>(num_pairs) >= num_tiles) ||
                         ((t + static_cast<int>(num_pairs)) % p.num_m_blocks != mb);
@@ -274,18 +287,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
         if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
       }
       const int row_base = row - static_cast<int>(lane);  // first row of this warp
-      const uint32_t taddr = tmem_base + acc * BN + ((q * 32u) << 16);
+      const uint32_t taddr = tmem_base + acc * C::TILE_N + ((q * 32u) << 16);
+      constexpr int NCHUNK = C::TILE_N / 64 + (C::TILE_N % 64 ? 1 : 0);
 #pragma unroll 1
-      for (int c = 0; c < BN / 64 + (BN % 64 ? 1 : 0); ++c) {
+      for (int c = 0; c < NCHUNK; ++c) {
         // 64 columns (the last chunk may be 32): TMEM -> fp32 -> scale/bias ->
         // bf16 into a 128B-swizzled [32 rows x 128 B] smem block, then each
         // quarter-warp writes one full 128-byte row segment to global.
-        const bool half = (c * 64 + 32 >= BN);
+        const bool half = (c * 64 + 32 >= C::TILE_N);
         uint32_t v[64];
         tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_ld_wait();
-        if (c == BN / 64 + (BN % 64 ? 1 : 0) - 1) {
+        if (c == NCHUNK - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
@@ -348,10 +362,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES>:
 
 // ------------------------------------------------------------------ host side
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, int NACC>
 static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
-  using C = PairCfg<BN, STAGES>;
-  auto kern = fused_rmsnorm_linear_pair_kernel<T, BN, STAGES>;
+  using C = PairCfg<BN, STAGES, NACC>;
+  auto kern = fused_rmsnorm_linear_pair_kernel<T, BN, STAGES, NACC>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
   static int max_pairs[kMaxDevices] = {};
@@ -372,7 +386,10 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
     qc.numAttrs = 1;
     int clusters = 0;
     e = cudaOccupancyMaxActiveClusters(&clusters, kern, &qc);
-    if (e != cudaSuccess || clusters <= 0) clusters = sm_count(dev) / 2;
+    if (e != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = sm_count(dev) / 2;
+    }
     max_pairs[dev] = clusters;
   }
   const int pairs_avail = dev < kMaxDevices ? max_pairs[dev] : sm_count(dev) / 2;
@@ -391,7 +408,7 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
   p.N = static_cast<int32_t>(pr.N);
   p.K = static_cast<int32_t>(pr.K);
   p.num_m_blocks = static_cast<int32_t>((pr.M + 2 * C::BM - 1) / (2 * C::BM));
-  p.num_n_blocks = static_cast<int32_t>((pr.N + BN - 1) / BN);
+  p.num_n_blocks = static_cast<int32_t>((pr.N + C::TILE_N - 1) / C::TILE_N);
   p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
   p.eps = pr.eps;
   p.bias = pr.bias;
@@ -416,37 +433,62 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
   return 0;
 }
 
-// Pair-tile width: minimise (pair tiles per pair) x BN over BN in {256, 224,
-// 192, 160, 128}; ties go to the wider tile (fewer W re-reads of x).
-int choose_pair_kernel(int64_t M, int64_t N, int pairs) {
-  const int64_t mb = (M + 255) / 256;
-  const int bns[5] = {256, 224, 192, 160, 128};
+// Pair-tile choice.  Per pair tile of 256 x (NACC*BN) over nkb 64-deep
+// k-blocks, in SM cycles:
+//   mma  = nkb * 2 * NACC * BN                 (two SMs, 4096 MAC/clk each)
+//   feed = nkb * (16 KB + NACC * BN * 64 B) / 60 B/clk   (measured L2->SM
+//          ceiling per SM when every SM loads tiles)
+//   epi  = 128 * NACC * BN * 2 B / 26 B/clk    (epilogue drain per CTA)
+// A tile costs max(mma, feed); with NACC = 1 the epilogue overlaps the next
+// tile and only the last one is exposed, with NACC = 2 every epilogue is.
+// The busiest pair runs ceil(tiles / pairs) tiles.
+PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs) {
+  const double mb = static_cast<double>((M + 255) / 256);
+  const double nkb = static_cast<double>((K + 63) / 64);
+  static const PairChoice cands[] = {{256, 1}, {224, 1}, {192, 1}, {160, 1}, {128, 1},
+                                     {256, 2}, {224, 2}, {192, 2}, {128, 2}};
   double best = 1e300;
-  int best_bn = 256;
-  for (int i = 0; i < 5; ++i) {
-    const int64_t tiles = mb * ((N + bns[i] - 1) / bns[i]);
-    const int64_t per_pair = (tiles + pairs - 1) / pairs;
-    const double cost = static_cast<double>(per_pair) * (bns[i] + 16);
-    if (cost < best - 1e-9) { best = cost; best_bn = bns[i]; }
+  PairChoice pick = {256, 1};
+  for (const PairChoice& c : cands) {
+    const double tn = static_cast<double>(c.nacc * c.bn);
+    const double tiles = mb * std::ceil(static_cast<double>(N) / tn);
+    const double per_pair = std::ceil(tiles / pairs);
+    const double mma = nkb * 2.0 * tn;
+    const double feed = nkb * (16384.0 + tn * 64.0) / 60.0;
+    const double epi = 128.0 * tn * 2.0 / 26.0;
+    const double tile = (mma > feed ? mma : feed) + (c.nacc == 2 ? epi : 0.0);
+    const double total = per_pair * tile + (c.nacc == 1 ? epi : 0.0);
+    if (total < best * 0.999) { best = total; pick = c; }
   }
-  return best_bn;
+  return pick;
 }
 
 template <typename T>
-static int run_pair_t(const LinearProblem& pr, int bn, cudaStream_t s) {
-  switch (bn) {
-    case 256: return launch_pair<T, 256, 6>(pr, s);
-    case 224: return launch_pair<T, 224, 6>(pr, s);
-    case 192: return launch_pair<T, 192, 6>(pr, s);
-    case 160: return launch_pair<T, 160, 6>(pr, s);
-    case 128: return launch_pair<T, 128, 8>(pr, s);
-    default: return set_error(FRN_ERR_INVALID_ARGUMENT, "unsupported pair tile width %d", bn);
+static int run_pair_t(const LinearProblem& pr, PairChoice c, cudaStream_t s) {
+  if (c.nacc == 2) {
+    switch (c.bn) {
+      case 256: return launch_pair<T, 256, 4, 2>(pr, s);
+      case 224: return launch_pair<T, 224, 4, 2>(pr, s);
+      case 192: return launch_pair<T, 192, 4, 2>(pr, s);
+      case 128: return launch_pair<T, 128, 6, 2>(pr, s);
+      default: break;
+    }
+  } else {
+    switch (c.bn) {
+      case 256: return launch_pair<T, 256, 6, 1>(pr, s);
+      case 224: return launch_pair<T, 224, 6, 1>(pr, s);
+      case 192: return launch_pair<T, 192, 6, 1>(pr, s);
+      case 160: return launch_pair<T, 160, 6, 1>(pr, s);
+      case 128: return launch_pair<T, 128, 8, 1>(pr, s);
+      default: break;
+    }
   }
+  return set_error(FRN_ERR_INVALID_ARGUMENT, "unsupported pair tiling %d x %d", c.nacc, c.bn);
 }
 
-int run_fused_linear_pair(const LinearProblem& pr, int bn, cudaStream_t s) {
-  if (pr.dtype == FRN_DTYPE_BF16) return run_pair_t<__nv_bfloat16>(pr, bn, s);
-  if (pr.dtype == FRN_DTYPE_F16) return run_pair_t<__half>(pr, bn, s);
+int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s) {
+  if (pr.dtype == FRN_DTYPE_BF16) return run_pair_t<__nv_bfloat16>(pr, c, s);
+  if (pr.dtype == FRN_DTYPE_F16) return run_pair_t<__half>(pr, c, s);
   return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+Linear supports bf16 and fp16 only");
 }
 

@@ -512,7 +512,7 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
 
 template <typename T>
 static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
-  const int bn = choose_pair_kernel(pr.M, pr.N, sm_count(0) / 2);
+  const int bn = choose_pair_tiling(pr.M, pr.N, pr.K, sm_count(0) / 2).bn;
   switch (bn) {
     case 256: return launch_w8<T, 256, 4>(pr, s);
     case 224: return launch_w8<T, 224, 4>(pr, s);

@@ -62,9 +62,13 @@ uint64_t wait_timeout_ns();
 
 int choose_prefill_kernel(int64_t M, int64_t N, int sms);
 int run_fused_linear_prefill(const LinearProblem& pr, int kernel, cudaStream_t s);
-// SM-pair (cta_group::2) kernel: `bn` is the pair tile width.
-int choose_pair_kernel(int64_t M, int64_t N, int pairs);
-int run_fused_linear_pair(const LinearProblem& pr, int bn, cudaStream_t s);
+// SM-pair (cta_group::2) kernel: a pair tile is 256 x (nacc * bn).
+struct PairChoice {
+  int bn;
+  int nacc;
+};
+PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs);
+int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s);
 // Decode (M <= 128) swap-AB kernel, `split` CTAs per cluster along K.
 int choose_decode_split(int64_t N, int64_t K, int sms);
 int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s);

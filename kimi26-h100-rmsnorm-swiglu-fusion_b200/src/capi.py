@@ -36,6 +36,10 @@ FRN_KERNEL_PAIR_N192 = 7
 FRN_KERNEL_PAIR_N224 = 8
 FRN_KERNEL_PAIR_N256 = 9
 FRN_KERNEL_PAIR_AUTO = 10
+FRN_KERNEL_WIDE_N128 = 11
+FRN_KERNEL_WIDE_N192 = 12
+FRN_KERNEL_WIDE_N224 = 13
+FRN_KERNEL_WIDE_N256 = 14
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {
