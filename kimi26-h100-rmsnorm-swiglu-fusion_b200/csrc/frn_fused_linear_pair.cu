@@ -8,8 +8,8 @@
 //
 // Roles (each CTA of the pair):
 //   warps 0-3   epilogue: TMEM lanes of this CTA's 128 rows -> acc * inv_rms
-//               + b -> one rounding -> swizzled smem block per warp -> full
-//               128-byte row segments stored to global (coalesced).
+//               + b -> one rounding -> swizzled smem block per warp -> TMA
+//               tensor store (double-buffered per warp).
 //   warps 4-7   TMA producers: x tile / W half-tile, each split over even and
 //               odd stages (four issuing threads, because one thread keeps
 //               only a few bulk-tensor loads in flight).  Both CTAs' loads
@@ -64,6 +64,8 @@ struct PairCfg {
   static constexpr uint32_t PAIR_TX = 2u * (A_BYTES + NACC * B_BYTES);
   static constexpr uint32_t TMEM_COLS = (NBUF * TILE_N <= 256) ? 256u : 512u;
   static constexpr int STG_BYTES = 32 * 128;  // one warp's 32 rows x 64 columns
+  static constexpr int NCHUNK = (TILE_N + 63) / 64;  // epilogue chunks of 64 columns
+  static constexpr bool HALF_TAIL = TILE_N % 64 != 0;  // last chunk is 32 columns
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_STG = OFF_B + STAGES * NACC * B_BYTES;
@@ -83,6 +85,7 @@ struct PairCfg {
   static_assert(NACC == 1 || NACC == 2, "NACC");
   static_assert(NBUF * TILE_N <= 512, "TMEM has 512 columns");
   static_assert(B_BYTES % 1024 == 0, "stage buffers must stay 1024-aligned");
+  static_assert(OFF_STG % 1024 == 0, "staging blocks must be 1024-aligned for the 128B swizzle");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
@@ -90,6 +93,8 @@ template <typename T, int BN, int STAGES, int NACC>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, NACC>::THREADS, 1)
     fused_rmsnorm_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                      const __grid_constant__ CUtensorMap tmap_w,
+                                     const __grid_constant__ CUtensorMap tmap_out,
+                                     const __grid_constant__ CUtensorMap tmap_out_half,
                                      const PairParams p) {
   using C = PairCfg<BN, STAGES, NACC>;
   extern __shared__ uint8_t smem_raw[];
@@ -117,6 +122,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
   if (warp == C::WARP_PROD0 && lane == 0) {
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_out);
+    if (C::HALF_TAIL) prefetch_tmap(&tmap_out_half);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&mma_done[s], 1);
@@ -260,9 +267,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
     // Epilogue: warp q owns TMEM lanes [32q, 32q+32) = rows of this CTA's half.
     const uint32_t q = warp;
     const bool has_bias = p.bias != nullptr;
-    const uint4* bias16 = reinterpret_cast<const uint4*>(p.bias);
+    const T* bias = static_cast<const T*>(p.bias);
     const uint32_t leader_tmem_empty0 = mapa_shared(smem_addr(&tmem_empty[0]), 0);
     griddep_wait();
+    uint32_t nst = 0;  // chunks this warp has staged: staging buffer nst & 1
     int i = 0;
     int gen = -1, cur_m = -1;
     float inv_rms = 0.f;
@@ -288,61 +296,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       }
       const int row_base = row - static_cast<int>(lane);  // first row of this warp
       const uint32_t taddr = tmem_base + acc * C::TILE_N + ((q * 32u) << 16);
-      constexpr int NCHUNK = C::TILE_N / 64 + (C::TILE_N % 64 ? 1 : 0);
 #pragma unroll 1
-      for (int c = 0; c < NCHUNK; ++c) {
+      for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
         // 64 columns (the last chunk may be 32): TMEM -> fp32 -> scale/bias ->
-        // bf16 into a 128B-swizzled [32 rows x 128 B] smem block, then each
-        // quarter-warp writes one full 128-byte row segment to global.
-        const bool half = (c * 64 + 32 >= C::TILE_N);
+        // one rounding -> swizzled smem block -> TMA store, which clips rows
+        // >= M and columns >= N.
+        const bool half = C::HALF_TAIL && c == C::NCHUNK - 1;
+        const int col0 = n0 + c * 64;
+        uint4 bv[8];
+        if (has_bias) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            bv[j] = (col0 + j * 8 < p.N && !(half && j >= 4))
+                        ? ld_global_nc_v4(bias + col0 + j * 8)
+                        : make_uint4(0u, 0u, 0u, 0u);
+        }
         uint32_t v[64];
         tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_ld_wait();
-        if (c == NCHUNK - 1) {
+        if (c == C::NCHUNK - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
         }
-        uint8_t* sb = smem + C::OFF_STG + (q * 2 + (c & 1)) * C::STG_BYTES;
-        const int col0 = n0 + c * 64;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {  // 16-byte chunk j = columns [8j, 8j+8)
-          if (half && j >= 4) break;
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) * inv_rms;
-          const int col = col0 + j * 8;
-          if (has_bias && col < p.N) {
-            const uint4 bv = __ldg(bias16 + col / 8);
-            const float2 b0 = pair_to_float2<T>(bv.x), b1 = pair_to_float2<T>(bv.y);
-            const float2 b2 = pair_to_float2<T>(bv.z), b3 = pair_to_float2<T>(bv.w);
-            f[0] += b0.x; f[1] += b0.y; f[2] += b1.x; f[3] += b1.y;
-            f[4] += b2.x; f[5] += b2.y; f[6] += b3.x; f[7] += b3.y;
-          }
-          uint4 o;
-          o.x = float2_to_pair<T>(f[0], f[1]);
-          o.y = float2_to_pair<T>(f[2], f[3]);
-          o.z = float2_to_pair<T>(f[4], f[5]);
-          o.w = float2_to_pair<T>(f[6], f[7]);
-          *reinterpret_cast<uint4*>(sb + lane * 128 + ((j ^ (lane & 7)) << 4)) = o;
-        }
+        uint8_t* sbp = smem + C::OFF_STG + (q * 2 + (nst & 1u)) * C::STG_BYTES;
+        const uint32_t sb = smem_addr(sbp);
+        // The TMA store issued two chunks ago read this buffer; at most the
+        // previous chunk's store may still be reading smem.
+        if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
-        // Read back: thread -> (row r = i*4 + lane/8, 16-byte chunk lane%8).
-        const int chunk = static_cast<int>(lane & 7);
-        const int col = col0 + chunk * 8;
-        const bool col_ok = col < p.N && !(half && chunk >= 4);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = i * 4 + static_cast<int>(lane >> 3);
-          const uint4 o = *reinterpret_cast<const uint4*>(sb + r * 128 + ((chunk ^ (r & 7)) << 4));
-          const int grow = row_base + r;
-          if (col_ok && grow < p.M)
-            st_global_v4(static_cast<T*>(p.out) + static_cast<int64_t>(grow) * p.out_row_stride + col,
-                         o.x, o.y, o.z, o.w);
+        if (half) {
+          if (has_bias) stage_rows_swizzled<T, 4, true>(v, inv_rms, bv, sb, lane);
+          else stage_rows_swizzled<T, 4, false>(v, inv_rms, bv, sb, lane);
+        } else {
+          if (has_bias) stage_rows_swizzled<T, 8, true>(v, inv_rms, bv, sb, lane);
+          else stage_rows_swizzled<T, 8, false>(v, inv_rms, bv, sb, lane);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(half ? &tmap_out_half : &tmap_out, sbp, col0, row_base);
+          bulk_commit_group();
         }
       }
     }
+    // Stores complete (not only their smem reads) before the CTA leaves.
+    if (lane == 0) bulk_wait_group_all();
   }
 
   // Every thread of both CTAs gets here (all waits are bounded), so the pair
@@ -402,6 +402,19 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
   rc = encode_tmap_2d(&tw, dt, 2, pr.w, pr.K, pr.N, pr.w_row_stride, C::BK, C::BN_HALF,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
+  // Output: one warp's [32 rows x 64 columns] block per store (128B swizzle),
+  // and [32 x 32] with the 64B swizzle for a tile whose last chunk is 32 wide.
+  CUtensorMap to, toh;
+  rc = encode_tmap_2d(&to, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 64, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (C::HALF_TAIL) {
+    rc = encode_tmap_2d(&toh, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  } else {
+    toh = to;
+  }
 
   PairParams p;
   p.M = static_cast<int32_t>(pr.M);
@@ -428,7 +441,7 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, to, toh, p);
   if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_pair", e);
   return 0;
 }

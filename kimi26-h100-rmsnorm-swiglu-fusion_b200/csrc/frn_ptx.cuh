@@ -321,6 +321,23 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// 16-byte store to this CTA's shared memory by shared-window address (keeps
+// the access an STS even where the compiler has lost the address space).
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d));
+}
+
+// 16-byte read-only global load (non-coherent path).
+__device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
@@ -407,6 +424,40 @@ template <>
 __device__ __forceinline__ uint32_t float2_to_pair<__half>(float a, float b) {
   __half2 r = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Epilogue staging for a TMA tensor store.  Lane r holds row r of a warp's
+// 32-row block as fp32 accumulator columns v[0 .. 8*NJ); each value is
+// multiplied by `scale` (the row's inv_rms), optionally gets the bias columns
+// bv[j] (8 values of T per 16-byte chunk) added, is rounded once to T, and is
+// written to the block at `sb` in the swizzled layout the store's tensor map
+// names:
+//   NJ = 8: rows of 128 B, 128-byte swizzle: chunk j of row r at
+//           r*128 + 16*(j ^ (r & 7))           (block 1024-byte aligned)
+//   NJ = 4: rows of 64 B, 64-byte swizzle:   chunk j of row r at
+//           r*64 + 16*(j ^ ((r >> 1) & 3))     (block 512-byte aligned)
+// Both patterns put the 8 lanes of each shared-memory phase on distinct banks.
+template <typename T, int NJ, bool BIAS>
+__device__ __forceinline__ void stage_rows_swizzled(const uint32_t (&v)[64], float scale,
+                                                    const uint4 (&bv)[8], uint32_t sb,
+                                                    uint32_t lane) {
+  static_assert(NJ == 8 || NJ == 4, "64- or 32-column blocks");
+#pragma unroll
+  for (int j = 0; j < NJ; ++j) {
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) * scale;
+    if (BIAS) {
+      const float2 b0 = pair_to_float2<T>(bv[j].x), b1 = pair_to_float2<T>(bv[j].y);
+      const float2 b2 = pair_to_float2<T>(bv[j].z), b3 = pair_to_float2<T>(bv[j].w);
+      f[0] += b0.x; f[1] += b0.y; f[2] += b1.x; f[3] += b1.y;
+      f[4] += b2.x; f[5] += b2.y; f[6] += b3.x; f[7] += b3.y;
+    }
+    const uint32_t off = NJ == 8 ? lane * 128u + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4)
+                                 : lane * 64u + ((static_cast<uint32_t>(j) ^ ((lane >> 1) & 3u)) << 4);
+    st_shared_v4(sb + off, float2_to_pair<T>(f[0], f[1]), float2_to_pair<T>(f[2], f[3]),
+                 float2_to_pair<T>(f[4], f[5]), float2_to_pair<T>(f[6], f[7]));
+  }
 }
 
 }  // namespace frn
