@@ -304,9 +304,11 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     }
   }
 
-  // Nobody leaves while a peer may still read its shared memory.
+  // Nobody leaves while a peer may still read its shared memory.  The peers'
+  // remote reads have all returned (their values are already stored), so
+  // the rendezvous needs no release.
   __syncwarp();
-  cluster_sync_all();
+  cluster_sync_relaxed();
   if (*abort_flag) __nanosleep(20000);
   if (warp == C::WARP_MMA) {
     tc_fence_after();

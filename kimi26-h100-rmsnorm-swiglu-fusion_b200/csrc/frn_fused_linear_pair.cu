@@ -145,7 +145,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
   }
   tc_fence_before();
   // Both CTAs' barriers must be initialised before either signals the other.
-  cluster_sync_all();
+  // __syncthreads publishes this CTA's inits and TMEM slot to its own
+  // threads; the peer's inits were released cluster-wide by its
+  // fence.mbarrier_init, so the cluster rendezvous itself is relaxed.
+  __syncthreads();
+  cluster_sync_relaxed();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -295,6 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
       }
       const int row_base = row - static_cast<int>(lane);  // first row of this warp
+      const bool reuse_acc = t + C::NBUF * static_cast<int>(num_pairs) < num_tiles;
       const uint32_t taddr = tmem_base + acc * C::TILE_N + ((q * 32u) << 16);
 #pragma unroll 1
       for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
@@ -315,7 +320,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_ld_wait();
-        if (c == C::NCHUNK - 1) {
+        if (c == C::NCHUNK - 1 && reuse_acc) {
+          // Only a later tile of this pair waits for this accumulator; the
+          // last NBUF tiles send nothing, so no remote arrive is in flight
+          // when the pair leaves.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
@@ -341,15 +349,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         }
       }
     }
-    // Stores complete (not only their smem reads) before the CTA leaves.
-    if (lane == 0) bulk_wait_group_all();
+    // The staging blocks must not be released while a store still reads them;
+    // the global writes themselves are complete when the grid is.
+    if (lane == 0) bulk_wait_group_read<0>();
   }
 
   // Every thread of both CTAs gets here (all waits are bounded), so the pair
-  // never leaves with the other CTA still reading its smem or barriers.
+  // never leaves with the other CTA still reading its smem or barriers.  Each
+  // cross-CTA signal (pair loads, multicast commits, accumulator releases) has
+  // been waited for by its target by now, so the rendezvous is relaxed.
   __syncwarp();
   tc_fence_before();
-  cluster_sync_all();
+  cluster_sync_relaxed();
   if (*abort_flag) {
     // A wait expired: give in-flight bulk copies into this CTA time to land.
     __nanosleep(20000);

@@ -261,6 +261,15 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// Cluster rendezvous without release semantics on the arrive.  For points
+// where every cross-CTA write of this thread has already been observed by its
+// target (or was released by a fence such as fence.mbarrier_init), so only
+// the execution barrier is needed; a releasing arrive costs a cluster-scope
+// memory fence while the SM still has global stores draining.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
 // 2-D tiled TMA load for a CTA pair: data lands in this CTA's smem, the
 // transaction bytes are signalled on `bar_cluster_addr`, which may be the
 // mbarrier of either CTA of the pair.
