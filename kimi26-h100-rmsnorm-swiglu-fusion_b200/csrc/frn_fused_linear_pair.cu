@@ -153,7 +153,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Each pair owns a contiguous run [t_begin, t_end) of the tiles in
+  // m-block-major order, so consecutive tiles of a pair mostly share their
+  // m-block and inv_rms is reduced once per run rather than once per tile.
   const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  const int tiles_base = num_tiles / static_cast<int>(num_pairs);
+  const int tiles_rem = num_tiles % static_cast<int>(num_pairs);
+  const int t_begin = static_cast<int>(pair) * tiles_base +
+                      min(static_cast<int>(pair), tiles_rem);
+  const int t_end = t_begin + tiles_base + (static_cast<int>(pair) < tiles_rem ? 1 : 0);
   const int nkb = p.num_k_blocks;
   const uint64_t to = p.timeout_ns;
   // Let the next kernel in the stream get scheduled now: its CTAs take SMs as
@@ -171,9 +179,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       const uint32_t parity_sel = pid >> 1;  // this thread fills stages with s % 2 == parity_sel
       const bool arms = is_a && rank == 0;
       uint32_t stage = 0, phase = 0;
-      for (int t = pair; t < num_tiles; t += num_pairs) {
-        const int m0 = (t % p.num_m_blocks) * 2 * C::BM + rank * C::BM;
-        const int n0 = (t / p.num_m_blocks) * C::TILE_N + rank * C::BN_HALF;
+      for (int t = t_begin; t < t_end; ++t) {
+        const int m0 = (t / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
+        const int n0 = (t % p.num_n_blocks) * C::TILE_N + rank * C::BN_HALF;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
           if ((stage & 1u) == parity_sel) {
@@ -200,7 +208,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       uint32_t stage = 0, phase = 0;
       int i = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+      for (int t = t_begin; t < t_end && ok; ++t, ++i) {
         const uint32_t acc = i % C::NBUF, acc_phase = (i / C::NBUF) & 1;
         if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) break;
         tc_fence_after();
@@ -237,8 +245,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
     uint32_t stage = 0, phase = 0;
     int gen = -1, cur_m = -1;
     bool ok = true;
-    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-      const int mb = t % p.num_m_blocks;
+    for (int t = t_begin; t < t_end && ok; ++t) {
+      const int mb = t / p.num_n_blocks;
       const bool first = (mb != cur_m);
       if (first) { ++gen; cur_m = mb; }
       float ss0 = 0.f, ss1 = 0.f;
@@ -278,14 +286,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
     int i = 0;
     int gen = -1, cur_m = -1;
     float inv_rms = 0.f;
-    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
+    for (int t = t_begin; t < t_end; ++t, ++i) {
       const uint32_t acc = i % C::NBUF, acc_phase = (i / C::NBUF) & 1;
-      const int mb = t % p.num_m_blocks;
+      const int mb = t / p.num_n_blocks;
       const int row = mb * 2 * C::BM + rank * C::BM + q * 32 + lane;
-      const int n0 = (t / p.num_m_blocks) * C::TILE_N;
+      const int n0 = (t % p.num_n_blocks) * C::TILE_N;
       const bool first = (mb != cur_m);
-      const bool last = (t + static_cast<int>(num_pairs) >= num_tiles) ||
-                        ((t + static_cast<int>(num_pairs)) % p.num_m_blocks != mb);
+      const bool last = (t + 1 >= t_end) || ((t + 1) / p.num_n_blocks != mb);
       if (first) { ++gen; cur_m = mb; }
       const uint32_t g = static_cast<uint32_t>(gen);
       if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) break;
@@ -299,7 +306,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
       }
       const int row_base = row - static_cast<int>(lane);  // first row of this warp
-      const bool reuse_acc = t + C::NBUF * static_cast<int>(num_pairs) < num_tiles;
+      const bool reuse_acc = t + C::NBUF < t_end;
       const uint32_t taddr = tmem_base + acc * C::TILE_N + ((q * 32u) << 16);
 #pragma unroll 1
       for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
