@@ -60,7 +60,10 @@ struct W8Cfg {
   static constexpr int OFF_Q = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_STG = OFF_Q + STAGES * Q_BYTES;
   static constexpr int OFF_RMS = OFF_STG + 4 * 2 * STG_BYTES;
-  static constexpr int OFF_BAR = OFF_RMS + 2 * BM * 4;
+  static constexpr int OFF_SCL = OFF_RMS + 2 * BM * 4;  // per epilogue warp: the tile's scale[n]
+  static constexpr int OFF_BAR = OFF_SCL + 4 * BN * 4;
+  static constexpr int NCHUNK = (BN + 63) / 64;  // epilogue chunks of 64 columns
+  static constexpr bool HALF_TAIL = BN % 64 != 0;
   static constexpr int NUM_BARS = 5 * STAGES + 9;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
@@ -70,6 +73,7 @@ struct W8Cfg {
   static_assert(BN_HALF <= 32 * CONV_WARPS, "one converter thread per W row");
   static_assert(STAGES % 2 == 0, "stages are split between two producers");
   static_assert(B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "stage buffers must stay aligned");
+  static_assert(OFF_STG % 1024 == 0, "staging blocks must be 1024-aligned for the 128B swizzle");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
@@ -90,6 +94,8 @@ template <typename T, int BN, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::THREADS, 1)
     fused_rmsnorm_linear_w8_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                    const __grid_constant__ CUtensorMap tmap_q,
+                                   const __grid_constant__ CUtensorMap tmap_out,
+                                   const __grid_constant__ CUtensorMap tmap_out_half,
                                    const W8Params p) {
   using C = W8Cfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -119,6 +125,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
   if (warp == C::WARP_PROD0 && lane == 0) {
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_q);
+    prefetch_tmap(&tmap_out);
+    if (C::HALF_TAIL) prefetch_tmap(&tmap_out_half);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&qfull[s], 1);
@@ -141,11 +149,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     tmem_relinquish_pair();
   }
   tc_fence_before();
-  cluster_sync_all();
+  // This CTA's inits and TMEM slot reach its own threads through
+  // __syncthreads; the peer's inits were released by its fence.mbarrier_init.
+  __syncthreads();
+  cluster_sync_relaxed();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Contiguous m-block-major tile run per pair (inv_rms once per run).
   const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  const int tiles_base = num_tiles / static_cast<int>(num_pairs);
+  const int tiles_rem = num_tiles % static_cast<int>(num_pairs);
+  const int t_begin = static_cast<int>(pair) * tiles_base +
+                      min(static_cast<int>(pair), tiles_rem);
+  const int t_end = t_begin + tiles_base + (static_cast<int>(pair) < tiles_rem ? 1 : 0);
   const int nkb = p.num_k_blocks;
   const uint64_t to = p.timeout_ns;
   // Let the next kernel in the stream get scheduled now: its CTAs take SMs as
@@ -160,9 +177,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
       griddep_wait();
       const uint32_t parity_sel = warp - C::WARP_PROD0;
       uint32_t stage = 0, phase = 0;
-      for (int t = pair; t < num_tiles; t += num_pairs) {
-        const int m0 = (t % p.num_m_blocks) * 2 * C::BM + rank * C::BM;
-        const int n0 = (t / p.num_m_blocks) * BN + rank * C::BN_HALF;
+      for (int t = t_begin; t < t_end; ++t) {
+        const int m0 = (t / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
+        const int n0 = (t % p.num_n_blocks) * BN + rank * C::BN_HALF;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
           if ((stage & 1u) == parity_sel) {
@@ -186,7 +203,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
       uint32_t stage = 0, phase = 0;
       int i = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+      for (int t = t_begin; t < t_end && ok; ++t, ++i) {
         const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
         if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) break;
         tc_fence_after();
@@ -218,7 +235,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
     uint32_t stage = 0, phase = 0;
     bool ok = true;
-    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+    for (int t = t_begin; t < t_end && ok; ++t) {
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
         if (j < C::BN_HALF) {
@@ -257,8 +274,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     uint32_t stage = 0, phase = 0;
     int gen = -1, cur_m = -1;
     bool ok = true;
-    for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-      const int mb = t % p.num_m_blocks;
+    for (int t = t_begin; t < t_end && ok; ++t) {
+      const int mb = t / p.num_n_blocks;
       const bool first = (mb != cur_m);
       if (first) { ++gen; cur_m = mb; }
       float ss0 = 0.f, ss1 = 0.f;
@@ -289,26 +306,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
       if (lane == 0) mbar_arrive(&rms_full[g & 1]);
     }
   } else {
-    // Epilogue warps 0-3 (same as the bf16 pair kernel, plus scale[n]).
+    // Epilogue warps 0-3 (as in the bf16 pair kernel, plus scale[n]).
     const uint32_t q = warp;
     const bool has_bias = p.bias != nullptr;
-    const uint4* bias16 = reinterpret_cast<const uint4*>(p.bias);
-    const float4* scale4 = reinterpret_cast<const float4*>(p.scale);
+    const T* bias = static_cast<const T*>(p.bias);
     const uint32_t leader_tmem_empty0 = mapa_shared(smem_addr(&tmem_empty[0]), 0);
+    const uint32_t scl = smem_addr(smem + C::OFF_SCL + q * BN * 4);  // this warp's scale[n0 ..)
     griddep_wait();
+    uint32_t nst = 0;  // chunks this warp has staged: staging buffer nst & 1
     int i = 0;
     int gen = -1, cur_m = -1;
     float inv_rms = 0.f;
-    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
+    for (int t = t_begin; t < t_end; ++t, ++i) {
       const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
-      const int mb = t % p.num_m_blocks;
+      const int mb = t / p.num_n_blocks;
       const int row_base = mb * 2 * C::BM + rank * C::BM + q * 32;
-      const int n0 = (t / p.num_m_blocks) * BN;
+      const int n0 = (t % p.num_n_blocks) * BN;
       const bool first = (mb != cur_m);
-      const bool last = (t + static_cast<int>(num_pairs) >= num_tiles) ||
-                        ((t + static_cast<int>(num_pairs)) % p.num_m_blocks != mb);
+      const bool last = (t + 1 >= t_end) || ((t + 1) / p.num_n_blocks != mb);
+      const bool reuse_acc = t + 2 < t_end;
       if (first) { ++gen; cur_m = mb; }
       const uint32_t g = static_cast<uint32_t>(gen);
+      // The tile's column scales (0 past N) into this warp's slice; N % 8 == 0,
+      // so a group of 4 columns is either wholly inside or wholly past N.
+      for (int c4 = static_cast<int>(lane); c4 < BN / 4; c4 += 32) {
+        const int col = n0 + c4 * 4;
+        uint4 sv = make_uint4(0u, 0u, 0u, 0u);
+        if (col < p.N) sv = ld_global_nc_v4(p.scale + col);
+        st_shared_v4(scl + c4 * 16, sv.x, sv.y, sv.z, sv.w);
+      }
+      __syncwarp();
       if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) break;
       if (first) {
         if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) break;
@@ -320,68 +347,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
         if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
       }
       const uint32_t taddr = tmem_base + acc * BN + ((q * 32u) << 16);
-      constexpr int NCHUNK = BN / 64 + (BN % 64 ? 1 : 0);
 #pragma unroll 1
-      for (int c = 0; c < NCHUNK; ++c) {
-        const bool half = (c * 64 + 32 >= BN);
+      for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
+        const bool half = C::HALF_TAIL && c == C::NCHUNK - 1;
+        const int col0 = n0 + c * 64;
+        uint4 bv[8];
+        if (has_bias) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            bv[j] = (col0 + j * 8 < p.N && !(half && j >= 4))
+                        ? ld_global_nc_v4(bias + col0 + j * 8)
+                        : make_uint4(0u, 0u, 0u, 0u);
+        }
         uint32_t v[64];
         tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_ld_wait();
-        if (c == NCHUNK - 1) {
+        if (c == C::NCHUNK - 1 && reuse_acc) {
+          // Only a later tile of this pair waits for this accumulator.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
         }
-        uint8_t* sb = smem + C::OFF_STG + (q * 2 + (c & 1)) * C::STG_BYTES;
-        const int col0 = n0 + c * 64;
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          if (half && jj >= 4) break;
-          const int col = col0 + jj * 8;
-          float f[8];
-          float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
-          if (col < p.N) {
-            s0 = __ldg(scale4 + col / 4);
-            s1 = __ldg(scale4 + col / 4 + 1);
-          }
-          const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[jj * 8 + e]) * inv_rms * sc[e];
-          if (has_bias && col < p.N) {
-            const uint4 bv = __ldg(bias16 + col / 8);
-            const float2 b0 = pair_to_float2<T>(bv.x), b1 = pair_to_float2<T>(bv.y);
-            const float2 b2 = pair_to_float2<T>(bv.z), b3 = pair_to_float2<T>(bv.w);
-            f[0] += b0.x; f[1] += b0.y; f[2] += b1.x; f[3] += b1.y;
-            f[4] += b2.x; f[5] += b2.y; f[6] += b3.x; f[7] += b3.y;
-          }
-          uint4 o;
-          o.x = float2_to_pair<T>(f[0], f[1]);
-          o.y = float2_to_pair<T>(f[2], f[3]);
-          o.z = float2_to_pair<T>(f[4], f[5]);
-          o.w = float2_to_pair<T>(f[6], f[7]);
-          *reinterpret_cast<uint4*>(sb + lane * 128 + ((jj ^ (lane & 7)) << 4)) = o;
-        }
+        uint8_t* sbp = smem + C::OFF_STG + (q * 2 + (nst & 1u)) * C::STG_BYTES;
+        const uint32_t sb = smem_addr(sbp);
+        if (lane == 0) bulk_wait_group_read<1>();
         __syncwarp();
-        const int chunk = static_cast<int>(lane & 7);
-        const int col = col0 + chunk * 8;
-        const bool col_ok = col < p.N && !(half && chunk >= 4);
-#pragma unroll
-        for (int ii = 0; ii < 8; ++ii) {
-          const int r = ii * 4 + static_cast<int>(lane >> 3);
-          const uint4 o = *reinterpret_cast<const uint4*>(sb + r * 128 + ((chunk ^ (r & 7)) << 4));
-          const int grow = row_base + r;
-          if (col_ok && grow < p.M)
-            st_global_v4(static_cast<T*>(p.out) + static_cast<int64_t>(grow) * p.out_row_stride + col,
-                         o.x, o.y, o.z, o.w);
+        const uint32_t cs = scl + c * 64 * 4;
+        if (half) {
+          if (has_bias) stage_rows_swizzled<T, 4, true, true>(v, inv_rms, bv, sb, lane, cs);
+          else stage_rows_swizzled<T, 4, false, true>(v, inv_rms, bv, sb, lane, cs);
+        } else {
+          if (has_bias) stage_rows_swizzled<T, 8, true, true>(v, inv_rms, bv, sb, lane, cs);
+          else stage_rows_swizzled<T, 8, false, true>(v, inv_rms, bv, sb, lane, cs);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(half ? &tmap_out_half : &tmap_out, sbp, col0, row_base);
+          bulk_commit_group();
         }
       }
     }
+    if (lane == 0) bulk_wait_group_read<0>();
   }
 
+  // Every cross-CTA signal has been waited for by its target by now.
   __syncwarp();
   tc_fence_before();
-  cluster_sync_all();
+  cluster_sync_relaxed();
   if (*abort_flag) __nanosleep(20000);
   if (warp == C::WARP_MMA) {
     tc_fence_after();
@@ -480,6 +494,17 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
   rc = encode_tmap_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, pr.wq, pr.K, pr.N, pr.wq_row_stride,
                       C::BK, C::BN_HALF, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
+  CUtensorMap to, toh;
+  rc = encode_tmap_2d(&to, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 64, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (C::HALF_TAIL) {
+    rc = encode_tmap_2d(&toh, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  } else {
+    toh = to;
+  }
   W8Params p;
   p.M = static_cast<int32_t>(pr.M);
   p.N = static_cast<int32_t>(pr.N);
@@ -505,7 +530,7 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tq, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tq, to, toh, p);
   if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_w8", e);
   return 0;
 }

@@ -338,6 +338,14 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                "r"(d));
 }
 
+__device__ __forceinline__ float4 ld_shared_v4f(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
 // 16-byte read-only global load (non-coherent path).
 __device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
   uint4 v;
@@ -437,25 +445,33 @@ __device__ __forceinline__ uint32_t float2_to_pair<__half>(float a, float b) {
 
 // Epilogue staging for a TMA tensor store.  Lane r holds row r of a warp's
 // 32-row block as fp32 accumulator columns v[0 .. 8*NJ); each value is
-// multiplied by `scale` (the row's inv_rms), optionally gets the bias columns
-// bv[j] (8 values of T per 16-byte chunk) added, is rounded once to T, and is
-// written to the block at `sb` in the swizzled layout the store's tensor map
-// names:
+// multiplied by `scale` (the row's inv_rms) and, with COLSCALE, by the
+// column's factor read from shared memory at `colscale` (8*NJ floats),
+// optionally gets the bias columns bv[j] (8 values of T per 16-byte chunk)
+// added, is rounded once to T, and is written to the block at `sb` in the
+// swizzled layout the store's tensor map names:
 //   NJ = 8: rows of 128 B, 128-byte swizzle: chunk j of row r at
 //           r*128 + 16*(j ^ (r & 7))           (block 1024-byte aligned)
 //   NJ = 4: rows of 64 B, 64-byte swizzle:   chunk j of row r at
 //           r*64 + 16*(j ^ ((r >> 1) & 3))     (block 512-byte aligned)
 // Both patterns put the 8 lanes of each shared-memory phase on distinct banks.
-template <typename T, int NJ, bool BIAS>
+template <typename T, int NJ, bool BIAS, bool COLSCALE = false>
 __device__ __forceinline__ void stage_rows_swizzled(const uint32_t (&v)[64], float scale,
                                                     const uint4 (&bv)[8], uint32_t sb,
-                                                    uint32_t lane) {
+                                                    uint32_t lane, uint32_t colscale = 0) {
   static_assert(NJ == 8 || NJ == 4, "64- or 32-column blocks");
 #pragma unroll
   for (int j = 0; j < NJ; ++j) {
     float f[8];
+    if (COLSCALE) {
+      const float4 c0 = ld_shared_v4f(colscale + j * 32), c1 = ld_shared_v4f(colscale + j * 32 + 16);
+      const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) * scale;
+      for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) * cs[e] * scale;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) * scale;
+    }
     if (BIAS) {
       const float2 b0 = pair_to_float2<T>(bv[j].x), b1 = pair_to_float2<T>(bv[j].y);
       const float2 b2 = pair_to_float2<T>(bv[j].z), b3 = pair_to_float2<T>(bv[j].w);
