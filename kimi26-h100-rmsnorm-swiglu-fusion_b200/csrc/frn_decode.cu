@@ -205,10 +205,10 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     for (int i = 0; i < nkb; ++i) {
       if (!mbar_wait(&full[stage], phase, abort_flag, to)) break;
       if (t < MP) {
-        const uint8_t* row = smem + C::OFF_X + stage * C::X_BYTES + t * 128;
+        const uint32_t row = smem_addr(smem + C::OFF_X + stage * C::X_BYTES) + t * 128;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (t & 7)) << 4));
+          const uint4 v = ld_shared_v4(row + ((q ^ (t & 7)) << 4));
           const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
           const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
           ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);

@@ -197,11 +197,11 @@ __global__ void __launch_bounds__(FusedLinearCfg<BN, STAGES>::THREADS, 1)
       float ss0 = 0.f, ss1 = 0.f;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
-        const uint8_t* row = smem + C::OFF_A + stage * C::A_BYTES + r * 128;
+        const uint32_t row = smem_addr(smem + C::OFF_A + stage * C::A_BYTES) + r * 128;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           // logical 16-byte chunk q of this row sits at physical chunk q ^ (r % 8)
-          const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (r & 7)) << 4));
+          const uint4 v = ld_shared_v4(row + ((q ^ (r & 7)) << 4));
           const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
           const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
           ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);

@@ -252,11 +252,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       float ss0 = 0.f, ss1 = 0.f;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
-        const uint8_t* row = smem + C::OFF_A + stage * C::A_BYTES + r * 128;
+        const uint32_t row = smem_addr(smem + C::OFF_A + stage * C::A_BYTES) + r * 128;
         if (first)
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (r & 7)) << 4));
+          const uint4 v = ld_shared_v4(row + ((q ^ (r & 7)) << 4));
           const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
           const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
           ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);

@@ -18,11 +18,11 @@
 // the even CTA's `full`), int8 W half-tile [BN/2 x 64] (TMA, 64B-swizzled,
 // completes on this CTA's `qfull`), and the bf16 copy of that half-tile that
 // the converter warps write in the UMMA 128B-swizzled K-major layout and then
-// announce on the even CTA's `conv` barrier (8 arrivals: 4 warps x 2 CTAs).
+// announce on the even CTA's `conv` barrier (2 arrivals: one warp per CTA).
 //
 // Roles (each CTA): warps 0-3 epilogue, warps 4-5 producers (x and int8 W of
 // even / odd stages), warp 6 MMA (even CTA) + TMEM owner, warps 7-10 RMS,
-// warps 11-14 converters (thread = W row of the half-tile).
+// warps 11-14 converters (warp = stage mod 4, lane = W rows of the half-tile).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -70,24 +70,48 @@ struct W8Cfg {
   static constexpr int EPI_WARPS = 4, RMS_WARPS = 4, CONV_WARPS = 4;
   static constexpr int WARP_PROD0 = 4, WARP_MMA = 6, WARP_RMS0 = 7, WARP_CONV0 = 11;
   static constexpr int THREADS = 32 * 15;
-  static_assert(BN_HALF <= 32 * CONV_WARPS, "one converter thread per W row");
   static_assert(STAGES % 2 == 0, "stages are split between two producers");
   static_assert(B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "stage buffers must stay aligned");
   static_assert(OFF_STG % 1024 == 0, "staging blocks must be 1024-aligned for the 128B swizzle");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
-// Four signed int8 (one 32-bit word) -> four exact fp32 values, without the
-// int->float converter: place the byte (biased by 128) in the low mantissa
-// bits of 2^23 and subtract 2^23 + 128 (the magic-number conversion used for
-// low-bit weight dequantization, e.g. Kim et al. 2022, "Who Says Elephants
-// Can't Run").
-__device__ __forceinline__ void s8x4_to_f32x4(uint32_t w, float (&f)[4]) {
+// Four signed int8 (one 32-bit word, |q| <= 127) -> four exact 16-bit values
+// of T as two packed pairs {q0, q1}, {q2, q3}.  No int->float converter:
+//  bf16: put byte q+128 in the low mantissa bits of 2^23 and subtract 2^23 +
+//        128 in fp32 (magic-number conversion, e.g. Kim et al. 2022, "Who Says
+//        Elephants Can't Run"; two lanes per add.rn.f32x2), then keep the top
+//        16 bits -- exact, because |q| <= 127 has at most 7 significant bits;
+//  fp16: the same with 2^10 in half precision (0x6400 | (q+128)) minus 1152,
+//        two lanes per sub.f16x2.
+template <typename T>
+__device__ __forceinline__ void widen_s8x4(uint32_t w, uint32_t& o01, uint32_t& o23);
+
+template <>
+__device__ __forceinline__ void widen_s8x4<__nv_bfloat16>(uint32_t w, uint32_t& o01,
+                                                          uint32_t& o23) {
   const uint32_t u = w ^ 0x80808080u;  // q + 128 in every byte
-  f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
-  f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
-  f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
-  f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+  uint64_t p01 = (static_cast<uint64_t>(__byte_perm(u, 0x4B000000u, 0x7651)) << 32) |
+                 __byte_perm(u, 0x4B000000u, 0x7650);
+  uint64_t p23 = (static_cast<uint64_t>(__byte_perm(u, 0x4B000000u, 0x7653)) << 32) |
+                 __byte_perm(u, 0x4B000000u, 0x7652);
+  const uint64_t bias = 0xCB000080CB000080ull;  // -(2^23 + 128) in both lanes
+  asm("add.rn.f32x2 %0, %0, %2;\n\tadd.rn.f32x2 %1, %1, %2;"
+      : "+l"(p01), "+l"(p23)
+      : "l"(bias));
+  o01 = __byte_perm(static_cast<uint32_t>(p01), static_cast<uint32_t>(p01 >> 32), 0x7632);
+  o23 = __byte_perm(static_cast<uint32_t>(p23), static_cast<uint32_t>(p23 >> 32), 0x7632);
+}
+
+template <>
+__device__ __forceinline__ void widen_s8x4<__half>(uint32_t w, uint32_t& o01, uint32_t& o23) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t h01 = __byte_perm(u, 0x64646464u, 0x4140);  // {1024 + u0, 1024 + u1}
+  const uint32_t h23 = __byte_perm(u, 0x64646464u, 0x4342);
+  const uint32_t c = 0x64806480u;                           // {1152, 1152}
+  asm("sub.rn.f16x2 %0, %2, %4;\n\tsub.rn.f16x2 %1, %3, %4;"
+      : "=r"(o01), "=r"(o23)
+      : "r"(h01), "r"(h23), "r"(c));
 }
 
 template <typename T, int BN, int STAGES>
@@ -130,7 +154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&qfull[s], 1);
-      mbar_init(&conv[s], 2 * C::CONV_WARPS);
+      mbar_init(&conv[s], 2);  // one converter warp per CTA
       mbar_init(&mma_done[s], 1);
       mbar_init(&empty[s], C::RMS_WARPS);
     }
@@ -230,41 +254,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
       mbar_wait(drain, 0, &zero, to);
     }
   } else if (warp >= C::WARP_CONV0) {
-    // Converter thread j widens row j of this CTA's int8 half-tile.
-    const int j = static_cast<int>(threadIdx.x) - C::WARP_CONV0 * 32;
+    // Converter warp cw widens the k-blocks held in stages s with
+    // s % CONV_WARPS == cw (so up to CONV_WARPS stages convert at once): lane l
+    // takes rows l, l+32, ... of this CTA's int8 half-tile, then lane 0
+    // publishes the stage on the even CTA's `conv` barrier (one arrival per
+    // CTA).
+    const uint32_t cw = warp - C::WARP_CONV0;
     const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
+    const uint32_t q0 = smem_addr(smem + C::OFF_Q), b0 = smem_addr(smem + C::OFF_B);
     uint32_t stage = 0, phase = 0;
     bool ok = true;
     for (int t = t_begin; t < t_end && ok; ++t) {
       for (int kb = 0; kb < nkb; ++kb) {
-        if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
-        if (j < C::BN_HALF) {
-          // int8 row j: 64 bytes, 64B-swizzled (16-byte chunk c at c ^ ((j >> 1) & 3)).
-          const uint8_t* qrow = smem + C::OFF_Q + stage * C::Q_BYTES + j * 64;
-          uint8_t* brow = smem + C::OFF_B + stage * C::B_BYTES + j * 128;
+        if (stage % C::CONV_WARPS == cw) {
+          if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
+          const uint32_t qs = q0 + stage * C::Q_BYTES, bs = b0 + stage * C::B_BYTES;
+#pragma unroll 1
+          for (uint32_t j = lane; j < static_cast<uint32_t>(C::BN_HALF); j += 32) {
+            // int8 row j: 64 bytes, 64B-swizzled (16-byte chunk c at c ^ ((j >> 1) & 3));
+            // bf16 row j: 128 bytes, 128B-swizzled (chunk c at c ^ (j & 7)).
+            uint4 w[4];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 w = *reinterpret_cast<const uint4*>(qrow + ((c ^ ((j >> 1) & 3)) << 4));
-            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+            for (uint32_t c = 0; c < 4; ++c)
+              w[c] = ld_shared_v4(qs + j * 64 + ((c ^ ((j >> 1) & 3u)) << 4));
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {  // 8 int8 -> one 16-byte bf16 chunk
-              float f[8];
-              s8x4_to_f32x4(ws[2 * h], *reinterpret_cast<float(*)[4]>(&f[0]));
-              s8x4_to_f32x4(ws[2 * h + 1], *reinterpret_cast<float(*)[4]>(&f[4]));
-              uint4 o;
-              o.x = float2_to_pair<T>(f[0], f[1]);
-              o.y = float2_to_pair<T>(f[2], f[3]);
-              o.z = float2_to_pair<T>(f[4], f[5]);
-              o.w = float2_to_pair<T>(f[6], f[7]);
-              const int chunk = c * 2 + h;  // 16-byte chunk of the bf16 row
-              *reinterpret_cast<uint4*>(brow + ((chunk ^ (j & 7)) << 4)) = o;
+            for (uint32_t c = 0; c < 4; ++c) {
+              uint32_t o[8];
+              widen_s8x4<T>(w[c].x, o[0], o[1]);
+              widen_s8x4<T>(w[c].y, o[2], o[3]);
+              widen_s8x4<T>(w[c].z, o[4], o[5]);
+              widen_s8x4<T>(w[c].w, o[6], o[7]);
+              st_shared_v4(bs + j * 128 + (((2 * c) ^ (j & 7u)) << 4), o[0], o[1], o[2], o[3]);
+              st_shared_v4(bs + j * 128 + (((2 * c + 1) ^ (j & 7u)) << 4), o[4], o[5], o[6], o[7]);
             }
           }
+          // The tensor cores (async proxy) read what was just written.
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(leader_conv0 + stage * 8);
         }
-        // The tensor cores (async proxy) read what was just written.
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(leader_conv0 + stage * 8);
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
     }
@@ -282,10 +310,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
         if (first) {
-          const uint8_t* row = smem + C::OFF_A + stage * C::A_BYTES + r * 128;
+          const uint32_t row = smem_addr(smem + C::OFF_A + stage * C::A_BYTES) + r * 128;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const uint4 v = *reinterpret_cast<const uint4*>(row + ((q ^ (r & 7)) << 4));
+            const uint4 v = ld_shared_v4(row + ((q ^ (r & 7)) << 4));
             const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
             const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
             ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
