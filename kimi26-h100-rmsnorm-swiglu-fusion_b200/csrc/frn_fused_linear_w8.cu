@@ -18,7 +18,8 @@
 // the even CTA's `full`), int8 W half-tile [BN/2 x 64] (TMA, 64B-swizzled,
 // completes on this CTA's `qfull`), and the bf16 copy of that half-tile that
 // the converter warps write in the UMMA 128B-swizzled K-major layout and then
-// announce on the even CTA's `conv` barrier (2 arrivals: one warp per CTA).
+// announce on the even CTA's `conv` barrier (its own converter arrives and
+// expects 4 bytes, which the odd CTA's converter sends with st.async).
 //
 // Roles (each CTA): warps 0-3 epilogue, warps 4-5 producers (x and int8 W of
 // even / odd stages), warp 6 MMA (even CTA) + TMEM owner, warps 7-10 RMS,
@@ -154,7 +155,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&qfull[s], 1);
-      mbar_init(&conv[s], 2);  // one converter warp per CTA
+      mbar_init(&conv[s], 1);  // even CTA's converter arrives; odd CTA's sends 4 tx bytes
       mbar_init(&mma_done[s], 1);
       mbar_init(&empty[s], C::RMS_WARPS);
     }
@@ -261,6 +262,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     // CTA).
     const uint32_t cw = warp - C::WARP_CONV0;
     const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
+    const uint32_t leader_sink = mapa_shared(smem_addr(tmem_slot + 2), 0);
     const uint32_t q0 = smem_addr(smem + C::OFF_Q), b0 = smem_addr(smem + C::OFF_B);
     uint32_t stage = 0, phase = 0;
     bool ok = true;
@@ -269,7 +271,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
         if (stage % C::CONV_WARPS == cw) {
           if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
           const uint32_t qs = q0 + stage * C::Q_BYTES, bs = b0 + stage * C::B_BYTES;
-#pragma unroll 1
+#pragma unroll 2
           for (uint32_t j = lane; j < static_cast<uint32_t>(C::BN_HALF); j += 32) {
             // int8 row j: 64 bytes, 64B-swizzled (16-byte chunk c at c ^ ((j >> 1) & 3));
             // bf16 row j: 128 bytes, 128B-swizzled (chunk c at c ^ (j & 7)).
@@ -288,10 +290,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
               st_shared_v4(bs + j * 128 + (((2 * c + 1) ^ (j & 7u)) << 4), o[4], o[5], o[6], o[7]);
             }
           }
-          // The tensor cores (async proxy) read what was just written.
+          // The tensor cores (async proxy) read what was just written.  The
+          // even CTA arrives locally and expects 4 bytes; the odd CTA sends
+          // them with st.async, whose complete_tx on the even CTA's barrier is
+          // a cluster-scope release that does not stall this warp (a
+          // releasing remote arrive costs a few hundred cycles here).
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(leader_conv0 + stage * 8);
+          if (lane == 0) {
+            if (rank == 0)
+              mbar_arrive_expect_tx(&conv[stage], 4u);
+            else
+              st_async_complete_tx(leader_sink, 1u, leader_conv0 + stage * 8);
+          }
         }
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }

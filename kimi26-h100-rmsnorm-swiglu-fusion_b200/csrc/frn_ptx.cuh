@@ -261,6 +261,20 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// 4-byte store into a peer CTA's shared memory whose completion is signalled
+// as 4 transaction bytes on the peer's mbarrier.  The complete_tx has
+// cluster-scope release semantics, so the peer thread that acquires that
+// barrier phase also sees this thread's earlier writes -- without this thread
+// waiting for them as a releasing remote arrive would.
+__device__ __forceinline__ void st_async_complete_tx(uint32_t remote_addr, uint32_t value,
+                                                     uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+          remote_addr),
+      "r"(value), "r"(remote_bar)
+      : "memory");
+}
+
 // Cluster rendezvous without release semantics on the arrive.  For points
 // where every cross-CTA write of this thread has already been observed by its
 // target (or was released by a fence such as fence.mbarrier_init), so only
