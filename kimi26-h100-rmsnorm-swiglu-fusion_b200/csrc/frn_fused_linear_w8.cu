@@ -235,7 +235,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
-          if (!mbar_wait_cluster(&conv[stage], phase, abort_flag, to)) { ok = false; break; }
+          // As for the pair's TMA loads (data in the odd CTA, complete_tx on this
+          // barrier), a CTA-scope wait suffices: the odd CTA's half arrives as
+          // an st.async complete_tx, itself ordered after that CTA's
+          // fence.proxy.async.  (A cluster-scope acquire here cost ~0.25 us
+          // per k-block on the critical path.)
+          if (!mbar_wait(&conv[stage], phase, abort_flag, to)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + C::OFF_A + stage * C::A_BYTES);
           const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * C::B_BYTES);
