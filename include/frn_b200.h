@@ -156,6 +156,41 @@ int frn_quantize_int8_per_channel(int dtype, const void* w, int64_t N, int64_t K
                                   float* scale, void* stream);
 
 /*
+ * RMSNorm + SwiGLU epilogue of a precomputed [gate | up] GEMM output
+ * raw_output[rows, 2*intermediate] (raw = x . W_combined^T):
+ *     g = raw[r, c] * inv_rms[r] + b_new[c]
+ *     u = raw[r, intermediate + c] * inv_rms[r] + b_new[intermediate + c]
+ *     output[r, c] = round(g / (1 + exp(-g)) * u)       for c < intermediate
+ * inv_rms as in frn_rmsnorm_normalize; b_new has 2*intermediate entries.
+ * Replaces rmsnorm_swiglu_cuda / rmsnorm_swiglu_512_cuda (reference
+ * csrc/denominator_kernel.cu:2037-2134, bound in csrc/denominator.cpp:152-213)
+ * and honours all three row strides.
+ */
+int frn_rmsnorm_swiglu(int dtype, const void* x, int64_t x_row_stride, const void* raw_output,
+                       int64_t raw_row_stride, void* output, int64_t out_row_stride,
+                       const void* b_new, int64_t rows, int64_t h, int64_t intermediate,
+                       float eps, int threads_per_row, void* stream);
+
+/*
+ * Fused RMSNorm -> [gate | up] projection -> SwiGLU in one kernel:
+ *     acc_g[m, c] = sum_k x[m,k] * Wc[c, k]
+ *     acc_u[m, c] = sum_k x[m,k] * Wc[intermediate + c, k]
+ *     out[m, c] = round(silu(acc_g * inv_rms[m] + b[c]) *
+ *                       (acc_u * inv_rms[m] + b[intermediate + c]))
+ * w_combined is the gamma-folded [gate; up] weight (2*intermediate rows of K),
+ * bias has 2*intermediate entries or is NULL; the [M, 2*intermediate] GEMM
+ * output is never written to memory.  bf16 / fp16; same layout rules as
+ * frn_fused_rmsnorm_linear with N = 2*intermediate (intermediate % 8 == 0).
+ * Replaces FusedRMSNormSwiGLUV1/V3.forward (reference
+ * src/fused_forward.py:254-313): F.linear(x, W_combined) followed by
+ * rmsnorm_swiglu(_512).
+ */
+int frn_fused_rmsnorm_swiglu(int dtype, const void* x, int64_t M, int64_t K,
+                             int64_t x_row_stride, const void* w_combined, int64_t intermediate,
+                             int64_t w_row_stride, const void* bias, float eps, void* out,
+                             int64_t out_row_stride, void* stream);
+
+/*
  * Reads (and optionally clears) the device error word of `device`, which
  * kernels set when a bounded wait expires instead of hanging.  Synchronous
  * with respect to the device's legacy default stream.

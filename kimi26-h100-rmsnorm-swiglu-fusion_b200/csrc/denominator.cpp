@@ -5,8 +5,9 @@
 // over the C ABI in include/frn_b200.h: tensors are checked the way the
 // reference's host launchers check them (csrc/denominator_kernel.cu:1999-2001,
 // same messages), then their pointers, row strides and the current CUDA stream
-// are handed to libfrn_b200.so.  New exports: fused_rmsnorm_linear (the
-// single-launch fused op) and device_error.
+// are handed to libfrn_b200.so.  New exports: fused_rmsnorm_linear and
+// fused_rmsnorm_swiglu (single-launch fused ops), the int8-weight path, and
+// device_error.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -67,6 +68,89 @@ void rmsnorm_normalize(const at::Tensor& x, at::Tensor raw_output, const at::Ten
 void rmsnorm_normalize_512(const at::Tensor& x, at::Tensor raw_output, const at::Tensor& b_new,
                            int64_t h, double eps) {
   rmsnorm_normalize_impl(x, raw_output, b_new, h, eps, 512, "rmsnorm_normalize_512");
+}
+
+void rmsnorm_swiglu_impl(const at::Tensor& x, const at::Tensor& raw_output, at::Tensor& output,
+                         const at::Tensor& b_new, int64_t h, int64_t intermediate, double eps,
+                         int threads, const char* name) {
+  TORCH_CHECK(x.dim() == 2, "x must be 2D");
+  TORCH_CHECK(raw_output.dim() == 2, "raw_output must be 2D");
+  TORCH_CHECK(output.dim() == 2, "output must be 2D");
+  TORCH_CHECK(x.is_cuda() && raw_output.is_cuda() && output.is_cuda() && b_new.is_cuda(),
+              "All tensors must be on CUDA");
+  const int dt = dtype_code(x);
+  TORCH_CHECK(dt >= 0, "Unsupported dtype for RMSNorm SwiGLU: only fp32, fp16, bf16 supported");
+  TORCH_CHECK(raw_output.scalar_type() == x.scalar_type() &&
+                  output.scalar_type() == x.scalar_type() && b_new.scalar_type() == x.scalar_type(),
+              "x, raw_output, output and b_new must share one dtype");
+  TORCH_CHECK(raw_output.size(0) == x.size(0) && output.size(0) == x.size(0),
+              "x, raw_output and output must have the same rows");
+  TORCH_CHECK(h == x.size(1), "h (", h, ") must equal x.size(1) (", x.size(1), ")");
+  TORCH_CHECK(raw_output.size(1) == 2 * intermediate, "raw_output must have 2*intermediate columns");
+  TORCH_CHECK(output.size(1) == intermediate, "output must have intermediate columns");
+  TORCH_CHECK(b_new.numel() == 2 * intermediate, "b_new must have 2*intermediate elements");
+  TORCH_CHECK(x.stride(1) == 1 && raw_output.stride(1) == 1 && output.stride(1) == 1,
+              "x, raw_output and output must have unit stride along their last dim");
+  const at::Tensor b = b_new.contiguous();
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(frn_rmsnorm_swiglu(dt, x.data_ptr(), x.stride(0), raw_output.data_ptr(),
+                              raw_output.stride(0), output.data_ptr(), output.stride(0),
+                              b.data_ptr(), x.size(0), h, intermediate, static_cast<float>(eps),
+                              threads, stream_of(x)),
+           name);
+}
+
+void rmsnorm_swiglu(const at::Tensor& x, const at::Tensor& raw_output, at::Tensor output,
+                    const at::Tensor& b_new, int64_t h, int64_t intermediate, double eps) {
+  rmsnorm_swiglu_impl(x, raw_output, output, b_new, h, intermediate, eps, 256, "rmsnorm_swiglu");
+}
+
+void rmsnorm_swiglu_512(const at::Tensor& x, const at::Tensor& raw_output, at::Tensor output,
+                        const at::Tensor& b_new, int64_t h, int64_t intermediate, double eps) {
+  rmsnorm_swiglu_impl(x, raw_output, output, b_new, h, intermediate, eps, 512,
+                      "rmsnorm_swiglu_512");
+}
+
+at::Tensor fused_rmsnorm_swiglu(const at::Tensor& x_in, const at::Tensor& w,
+                                const c10::optional<at::Tensor>& b_combined, double eps,
+                                c10::optional<at::Tensor> out) {
+  TORCH_CHECK(x_in.dim() == 2, "x must be 2D");
+  TORCH_CHECK(w.dim() == 2, "W_combined must be 2D");
+  TORCH_CHECK(x_in.is_cuda() && w.is_cuda() && (!b_combined || b_combined->is_cuda()),
+              "All tensors must be on CUDA");
+  TORCH_CHECK(x_in.scalar_type() == at::kBFloat16 || x_in.scalar_type() == at::kHalf,
+              "fused_rmsnorm_swiglu supports bf16 and fp16 (got ", x_in.scalar_type(), ")");
+  TORCH_CHECK(w.scalar_type() == x_in.scalar_type(), "x and W_combined must share one dtype");
+  TORCH_CHECK(x_in.size(1) == w.size(1), "x.size(1) (", x_in.size(1),
+              ") != W_combined.size(1) (", w.size(1), ")");
+  TORCH_CHECK(w.size(0) % 2 == 0, "W_combined must have 2*intermediate rows");
+  TORCH_CHECK(x_in.device() == w.device(), "x and W_combined must be on the same device");
+  const at::Tensor x = (x_in.stride(1) == 1 || x_in.size(1) == 1) ? x_in : x_in.contiguous();
+  const at::Tensor wc = (w.stride(1) == 1) ? w : w.contiguous();
+  const int64_t M = x.size(0), K = x.size(1), I = wc.size(0) / 2;
+  at::Tensor b;
+  const void* bptr = nullptr;
+  if (b_combined && b_combined->defined()) {
+    TORCH_CHECK(b_combined->scalar_type() == x.scalar_type(), "b_combined must share x's dtype");
+    TORCH_CHECK(b_combined->numel() == 2 * I, "b_combined must have W_combined.size(0) elements");
+    b = b_combined->contiguous();
+    bptr = b.data_ptr();
+  }
+  at::Tensor o;
+  if (out && out->defined()) {
+    o = *out;
+    TORCH_CHECK(o.dim() == 2 && o.size(0) == M && o.size(1) == I, "out must be [M, intermediate]");
+    TORCH_CHECK(o.scalar_type() == x.scalar_type() && o.is_cuda(), "out dtype/device mismatch");
+    TORCH_CHECK(o.stride(1) == 1, "out must have unit stride along its last dim");
+  } else {
+    o = at::empty({M, I}, x.options());
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(frn_fused_rmsnorm_swiglu(dtype_code(x), x.data_ptr(), M, K, x.stride(0), wc.data_ptr(),
+                                    I, wc.stride(0), bptr, static_cast<float>(eps), o.data_ptr(),
+                                    o.stride(0), stream_of(x)),
+           "fused_rmsnorm_swiglu");
+  return o;
 }
 
 at::Tensor fused_rmsnorm_linear(const at::Tensor& x_in, const at::Tensor& w,
@@ -208,6 +292,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_normalize_512", &rmsnorm_normalize_512,
         "In-place RMSNorm rescale of a GEMM output (512 threads per row)", py::arg("x"),
         py::arg("raw_output"), py::arg("b_new"), py::arg("h"), py::arg("eps"));
+  m.def("rmsnorm_swiglu", &rmsnorm_swiglu,
+        "RMSNorm + SwiGLU of a [gate | up] GEMM output into output (256 threads per row)",
+        py::arg("x"), py::arg("raw_output"), py::arg("output"), py::arg("b_new"), py::arg("h"),
+        py::arg("intermediate"), py::arg("eps"));
+  m.def("rmsnorm_swiglu_512", &rmsnorm_swiglu_512,
+        "RMSNorm + SwiGLU of a [gate | up] GEMM output into output (512 threads per row)",
+        py::arg("x"), py::arg("raw_output"), py::arg("output"), py::arg("b_new"), py::arg("h"),
+        py::arg("intermediate"), py::arg("eps"));
+  m.def("fused_rmsnorm_swiglu", &fused_rmsnorm_swiglu,
+        "silu(r * (x @ Wg.T) + bg) * (r * (x @ Wu.T) + bu), r = rsqrt(mean(x^2)+eps); one launch",
+        py::arg("x"), py::arg("W_combined"), py::arg("b_combined") = py::none(),
+        py::arg("eps") = 1e-6, py::arg("out") = py::none());
   m.def("fused_rmsnorm_linear", &fused_rmsnorm_linear,
         "out = rsqrt(mean(x^2)+eps)[:,None] * (x @ W_fused.T) + b_new, one tcgen05 launch",
         py::arg("x"), py::arg("W_fused"), py::arg("b_new") = py::none(), py::arg("eps") = 1e-6,

@@ -161,6 +161,57 @@ int frn_rmsnorm_normalize(int dtype, const void* x, int64_t x_row_stride, void* 
                                static_cast<cudaStream_t>(stream));
 }
 
+int frn_rmsnorm_swiglu(int dtype, const void* x, int64_t x_row_stride, const void* raw_output,
+                       int64_t raw_row_stride, void* output, int64_t out_row_stride,
+                       const void* b_new, int64_t rows, int64_t h, int64_t intermediate,
+                       float eps, int threads_per_row, void* stream) {
+  if (dtype != FRN_DTYPE_F32 && dtype != FRN_DTYPE_F16 && dtype != FRN_DTYPE_BF16)
+    return set_error(FRN_ERR_UNSUPPORTED,
+                     "Unsupported dtype for RMSNorm SwiGLU: only fp32, fp16, bf16 supported");
+  if (rows < 0 || h <= 0 || intermediate < 0)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "bad shape rows=%lld h=%lld intermediate=%lld",
+                     (long long)rows, (long long)h, (long long)intermediate);
+  if (threads_per_row != 256 && threads_per_row != 512)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "threads_per_row must be 256 or 512");
+  if (rows == 0 || intermediate == 0) return FRN_OK;
+  if (!x || !raw_output || !output || !b_new)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "x, raw_output, output and b_new must be non-null");
+  if (x_row_stride < h || raw_row_stride < 2 * intermediate || out_row_stride < intermediate)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "row strides must be >= row lengths");
+  if (rows > 0x7fffffffLL || h > 0x7fffffffLL || 2 * intermediate > 0x7fffffffLL)
+    return set_error(FRN_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
+  return run_rmsnorm_swiglu(dtype, x, x_row_stride, raw_output, raw_row_stride, output,
+                            out_row_stride, b_new, rows, h, intermediate, eps, threads_per_row,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int frn_fused_rmsnorm_swiglu(int dtype, const void* x, int64_t M, int64_t K,
+                             int64_t x_row_stride, const void* w_combined, int64_t intermediate,
+                             int64_t w_row_stride, const void* bias, float eps, void* out,
+                             int64_t out_row_stride, void* stream) {
+  if (intermediate <= 0)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "bad intermediate size %lld",
+                     (long long)intermediate);
+  if (out_row_stride < intermediate)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "out row stride %lld < intermediate %lld",
+                     (long long)out_row_stride, (long long)intermediate);
+  // Validated as the [M, 2*intermediate] linear over W_combined; the output
+  // stride is checked against its own width above.
+  LinearProblem p{dtype, x, M, K, x_row_stride, w_combined, 2 * intermediate, w_row_stride,
+                  bias, eps, out, 2 * intermediate, nullptr, 0};
+  int rc = validate_linear(p);
+  if (rc) return rc;
+  if (out_row_stride % 8)
+    return set_error(FRN_ERR_MISALIGNED, "row strides must be multiples of 8 elements (16 bytes)");
+  p.out_row_stride = out_row_stride;
+  if (M == 0) return FRN_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  const int pairs = sm_count(dev) / 2;
+  return run_fused_swiglu_pair(p, intermediate, choose_swiglu_bn(M, intermediate, K, pairs),
+                               static_cast<cudaStream_t>(stream));
+}
+
 size_t frn_fused_rmsnorm_linear_workspace_size(int dtype, int64_t M, int64_t N, int64_t K) {
   (void)dtype; (void)M; (void)N; (void)K;
   return 0;

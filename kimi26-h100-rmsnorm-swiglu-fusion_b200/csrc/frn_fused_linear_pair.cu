@@ -45,6 +45,7 @@ struct PairParams {
   const void* bias;  // may be null
   void* out;
   int64_t out_row_stride;  // elements
+  int32_t up_row0;         // SwiGLU: first W row of the up block (= intermediate)
   uint64_t timeout_ns;
 };
 
@@ -89,7 +90,10 @@ struct PairCfg {
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
-template <typename T, int BN, int STAGES, int NACC>
+// SWIGLU (with NACC = 2): accumulator 0 holds x.W_gate^T for output columns
+// [n0, n0+BN), accumulator 1 x.W_up^T for the same columns (W rows up_row0 +
+// n), and the epilogue writes silu(g * inv_rms + b_g) * (u * inv_rms + b_u).
+template <typename T, int BN, int STAGES, int NACC, bool SWIGLU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, NACC>::THREADS, 1)
     fused_rmsnorm_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                      const __grid_constant__ CUtensorMap tmap_w,
@@ -97,6 +101,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
                                      const __grid_constant__ CUtensorMap tmap_out_half,
                                      const PairParams p) {
   using C = PairCfg<BN, STAGES, NACC>;
+  static_assert(!SWIGLU || NACC == 2, "the SwiGLU epilogue pairs the two accumulators");
+  constexpr int OUT_N = SWIGLU ? BN : C::TILE_N;  // output columns per pair tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -123,7 +129,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_out);
-    if (C::HALF_TAIL) prefetch_tmap(&tmap_out_half);
+    if (OUT_N % 64 != 0) prefetch_tmap(&tmap_out_half);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&mma_done[s], 1);
@@ -181,7 +187,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       uint32_t stage = 0, phase = 0;
       for (int t = t_begin; t < t_end; ++t) {
         const int m0 = (t / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
-        const int n0 = (t % p.num_n_blocks) * C::TILE_N + rank * C::BN_HALF;
+        const int n0 = (t % p.num_n_blocks) * OUT_N + rank * C::BN_HALF;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
           if ((stage & 1u) == parity_sel) {
@@ -195,7 +201,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
 #pragma unroll
               for (int j = 0; j < NACC; ++j)
                 tma_load_2d_pair(smem + C::OFF_B + (stage * NACC + j) * C::B_BYTES, &tmap_w,
-                                 leader_full, kb * C::BK, n0 + j * BN);
+                                 leader_full, kb * C::BK,
+                                 SWIGLU ? (j == 0 ? n0 : p.up_row0 + n0) : n0 + j * BN);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -290,7 +297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       const uint32_t acc = i % C::NBUF, acc_phase = (i / C::NBUF) & 1;
       const int mb = t / p.num_n_blocks;
       const int row = mb * 2 * C::BM + rank * C::BM + q * 32 + lane;
-      const int n0 = (t % p.num_n_blocks) * C::TILE_N;
+      const int n0 = (t % p.num_n_blocks) * OUT_N;
       const bool first = (mb != cur_m);
       const bool last = (t + 1 >= t_end) || ((t + 1) / p.num_n_blocks != mb);
       if (first) { ++gen; cur_m = mb; }
@@ -307,6 +314,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
       }
       const int row_base = row - static_cast<int>(lane);  // first row of this warp
       const bool reuse_acc = t + C::NBUF < t_end;
+      if constexpr (SWIGLU) {
+        constexpr int NCH = (BN + 63) / 64;
+        constexpr bool HALF = BN % 64 != 0;
+        const uint32_t tg = tmem_base + ((q * 32u) << 16);  // gate accumulator
+        const uint32_t tu = tg + BN;                        // up accumulator
+#pragma unroll 1
+        for (int c = 0; c < NCH; ++c, ++nst) {
+          const bool half = HALF && c == NCH - 1;
+          const int col0 = n0 + c * 64;
+          uint8_t* sbp = smem + C::OFF_STG + (q * 2 + (nst & 1u)) * C::STG_BYTES;
+          const uint32_t sb = smem_addr(sbp);
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+#pragma unroll 1
+          for (int h = 0; h < (half ? 1 : 2); ++h) {
+            // 32 output columns: gate and up accumulators side by side.
+            const int colh = col0 + h * 32;
+            uint4 bg[4], bu[4];
+            if (has_bias) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const bool in = colh + j * 8 < p.N;
+                bg[j] = in ? ld_global_nc_v4(bias + colh + j * 8) : make_uint4(0u, 0u, 0u, 0u);
+                bu[j] = in ? ld_global_nc_v4(bias + p.up_row0 + colh + j * 8)
+                           : make_uint4(0u, 0u, 0u, 0u);
+              }
+            }
+            uint32_t gv[32], uv[32];
+            tmem_ld_32x32b_x32(tg + c * 64 + h * 32, gv);
+            tmem_ld_32x32b_x32(tu + c * 64 + h * 32, uv);
+            tmem_ld_wait();
+            if (c == NCH - 1 && (half || h == 1) && reuse_acc) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0);
+            }
+            if (half) {
+              if (has_bias) stage_swiglu_rows<T, 4, true>(gv, uv, inv_rms, bg, bu, sb, lane, 0);
+              else stage_swiglu_rows<T, 4, false>(gv, uv, inv_rms, bg, bu, sb, lane, 0);
+            } else {
+              if (has_bias) stage_swiglu_rows<T, 8, true>(gv, uv, inv_rms, bg, bu, sb, lane, h * 4);
+              else stage_swiglu_rows<T, 8, false>(gv, uv, inv_rms, bg, bu, sb, lane, h * 4);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(half ? &tmap_out_half : &tmap_out, sbp, col0, row_base);
+            bulk_commit_group();
+          }
+        }
+        continue;
+      }
       const uint32_t taddr = tmem_base + acc * C::TILE_N + ((q * 32u) << 16);
 #pragma unroll 1
       for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
@@ -380,10 +440,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
 
 // ------------------------------------------------------------------ host side
 
-template <typename T, int BN, int STAGES, int NACC>
-static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
+// SWIGLU: pr.w holds [gate; up] (pr.N = 2 * inter rows) and the output has
+// `inter` columns.
+template <typename T, int BN, int STAGES, int NACC, bool SWIGLU = false>
+static int launch_pair(const LinearProblem& pr, cudaStream_t stream, int64_t inter = 0) {
   using C = PairCfg<BN, STAGES, NACC>;
-  auto kern = fused_rmsnorm_linear_pair_kernel<T, BN, STAGES, NACC>;
+  constexpr int OUT_N = SWIGLU ? BN : C::TILE_N;
+  const int64_t n_out = SWIGLU ? inter : pr.N;
+  auto kern = fused_rmsnorm_linear_pair_kernel<T, BN, STAGES, NACC, SWIGLU>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
   static int max_pairs[kMaxDevices] = {};
@@ -423,11 +487,11 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
   // Output: one warp's [32 rows x 64 columns] block per store (128B swizzle),
   // and [32 x 32] with the 64B swizzle for a tile whose last chunk is 32 wide.
   CUtensorMap to, toh;
-  rc = encode_tmap_2d(&to, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 64, 32,
+  rc = encode_tmap_2d(&to, dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 64, 32,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  if (C::HALF_TAIL) {
-    rc = encode_tmap_2d(&toh, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 32, 32,
+  if (OUT_N % 64 != 0) {
+    rc = encode_tmap_2d(&toh, dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 32, 32,
                         CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
   } else {
@@ -436,15 +500,16 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream) {
 
   PairParams p;
   p.M = static_cast<int32_t>(pr.M);
-  p.N = static_cast<int32_t>(pr.N);
+  p.N = static_cast<int32_t>(n_out);
   p.K = static_cast<int32_t>(pr.K);
   p.num_m_blocks = static_cast<int32_t>((pr.M + 2 * C::BM - 1) / (2 * C::BM));
-  p.num_n_blocks = static_cast<int32_t>((pr.N + C::TILE_N - 1) / C::TILE_N);
+  p.num_n_blocks = static_cast<int32_t>((n_out + OUT_N - 1) / OUT_N);
   p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
   p.eps = pr.eps;
   p.bias = pr.bias;
   p.out = pr.out;
   p.out_row_stride = pr.out_row_stride;
+  p.up_row0 = static_cast<int32_t>(inter);
   p.timeout_ns = wait_timeout_ns();
   const int tiles = p.num_m_blocks * p.num_n_blocks;
   const int pairs = tiles < pairs_avail ? tiles : pairs_avail;
@@ -521,6 +586,45 @@ int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s)
   if (pr.dtype == FRN_DTYPE_BF16) return run_pair_t<__nv_bfloat16>(pr, c, s);
   if (pr.dtype == FRN_DTYPE_F16) return run_pair_t<__half>(pr, c, s);
   return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+Linear supports bf16 and fp16 only");
+}
+
+// SwiGLU output-tile width (tile = 256 rows x bn output columns over two
+// bn-wide accumulators, gate and up): the cost model of choose_pair_tiling
+// with 2*bn columns of MMA per tile and every epilogue exposed.
+int choose_swiglu_bn(int64_t M, int64_t inter, int64_t K, int pairs) {
+  const double mb = static_cast<double>((M + 255) / 256);
+  const double nkb = static_cast<double>((K + 63) / 64);
+  static const int cands[] = {256, 224, 192, 128};
+  double best = 1e300;
+  int pick = 256;
+  for (int bn : cands) {
+    const double tiles = mb * std::ceil(static_cast<double>(inter) / bn);
+    const double per_pair = std::ceil(tiles / pairs);
+    const double mma = nkb * 2.0 * (2.0 * bn);
+    const double feed = nkb * (16384.0 + 2.0 * bn * 64.0) / 60.0;
+    const double epi = 128.0 * bn * 2.0 / 26.0;
+    const double total = per_pair * ((mma > feed ? mma : feed) + epi);
+    if (total < best * 0.999) { best = total; pick = bn; }
+  }
+  return pick;
+}
+
+template <typename T>
+static int run_swiglu_t(const LinearProblem& pr, int64_t inter, int bn, cudaStream_t s) {
+  switch (bn) {
+    case 256: return launch_pair<T, 256, 4, 2, true>(pr, s, inter);
+    case 224: return launch_pair<T, 224, 4, 2, true>(pr, s, inter);
+    case 192: return launch_pair<T, 192, 4, 2, true>(pr, s, inter);
+    case 128: return launch_pair<T, 128, 6, 2, true>(pr, s, inter);
+    default: break;
+  }
+  return set_error(FRN_ERR_INVALID_ARGUMENT, "unsupported SwiGLU tile width %d", bn);
+}
+
+int run_fused_swiglu_pair(const LinearProblem& pr, int64_t inter, int bn, cudaStream_t s) {
+  if (pr.dtype == FRN_DTYPE_BF16) return run_swiglu_t<__nv_bfloat16>(pr, inter, bn, s);
+  if (pr.dtype == FRN_DTYPE_F16) return run_swiglu_t<__half>(pr, inter, bn, s);
+  return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+SwiGLU supports bf16 and fp16 only");
 }
 
 }  // namespace frn

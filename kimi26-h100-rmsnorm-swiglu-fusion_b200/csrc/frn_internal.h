@@ -69,6 +69,10 @@ struct PairChoice {
 };
 PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs);
 int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s);
+// SwiGLU on the pair kernel: pr.w = [gate; up] with pr.N = 2 * inter rows;
+// the output has `inter` columns; tiles are 256 x bn output columns.
+int choose_swiglu_bn(int64_t M, int64_t inter, int64_t K, int pairs);
+int run_fused_swiglu_pair(const LinearProblem& pr, int64_t inter, int bn, cudaStream_t s);
 // Decode (M <= 128) swap-AB kernel, `split` CTAs per cluster along K.
 int choose_decode_split(int64_t N, int64_t K, int sms);
 int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s);
@@ -77,6 +81,9 @@ int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s);
 int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws, void* q,
                       int64_t qs, float* scale, cudaStream_t s);
 
+int run_rmsnorm_swiglu(int dtype, const void* x, int64_t xs, const void* raw, int64_t rs,
+                       void* out, int64_t os, const void* b, int64_t rows, int64_t h,
+                       int64_t inter, float eps, int threads, cudaStream_t s);
 int run_rmsnorm_normalize(int dtype, const void* x, int64_t xs, void* out, int64_t os,
                           const void* b, int64_t rows, int64_t h, int64_t n, float eps,
                           int threads, cudaStream_t s);

@@ -507,4 +507,44 @@ __device__ __forceinline__ void stage_rows_swizzled(const uint32_t (&v)[64], flo
   }
 }
 
+// SwiGLU variant: 32 columns of the gate (gv) and up (uv) accumulators of the
+// lane's row -> silu(g * scale + b_g) * (u * scale + b_u), rounded once to T,
+// written as 16-byte chunks jbase .. jbase+3 of the row in the same swizzled
+// layouts as stage_rows_swizzled (NJ = 8: 128-byte rows, NJ = 4: 64-byte).
+// silu(a) = a / (1 + e^-a), with the fast exponential and division.
+template <typename T, int NJ, bool BIAS>
+__device__ __forceinline__ void stage_swiglu_rows(const uint32_t (&gv)[32],
+                                                  const uint32_t (&uv)[32], float scale,
+                                                  const uint4 (&bg)[4], const uint4 (&bu)[4],
+                                                  uint32_t sb, uint32_t lane, int jbase) {
+  static_assert(NJ == 8 || NJ == 4, "64- or 32-column blocks");
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float g[8], u[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      g[e] = __uint_as_float(gv[j * 8 + e]) * scale;
+      u[e] = __uint_as_float(uv[j * 8 + e]) * scale;
+    }
+    if (BIAS) {
+      const uint32_t bgw[4] = {bg[j].x, bg[j].y, bg[j].z, bg[j].w};
+      const uint32_t buw[4] = {bu[j].x, bu[j].y, bu[j].z, bu[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = pair_to_float2<T>(bgw[e]), b = pair_to_float2<T>(buw[e]);
+        g[2 * e] += a.x; g[2 * e + 1] += a.y;
+        u[2 * e] += b.x; u[2 * e + 1] += b.y;
+      }
+    }
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = __fdividef(g[e], 1.0f + __expf(-g[e])) * u[e];
+    const uint32_t jj = static_cast<uint32_t>(jbase + j);
+    const uint32_t off = NJ == 8 ? lane * 128u + ((jj ^ (lane & 7u)) << 4)
+                                 : lane * 64u + ((jj ^ ((lane >> 1) & 3u)) << 4);
+    st_shared_v4(sb + off, float2_to_pair<T>(f[0], f[1]), float2_to_pair<T>(f[2], f[3]),
+                 float2_to_pair<T>(f[4], f[5]), float2_to_pair<T>(f[6], f[7]));
+  }
+}
+
 }  // namespace frn

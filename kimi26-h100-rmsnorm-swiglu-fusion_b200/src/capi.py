@@ -70,6 +70,16 @@ PROTOTYPES = {
         c_int,
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     ),
+    "frn_rmsnorm_swiglu": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+         c_int64, c_int64, c_float, c_int, c_void_p],
+    ),
+    "frn_fused_rmsnorm_swiglu": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+         c_float, c_void_p, c_int64, c_void_p],
+    ),
     "frn_device_error": (c_int, [c_int, ctypes.POINTER(c_uint32), c_int]),
 }
 
@@ -187,6 +197,39 @@ def quantize_int8_per_channel(w):
                                              _stream_ptr(w.device))
     check(rc, "frn_quantize_int8_per_channel")
     return q, scale
+
+
+def rmsnorm_swiglu(x, raw_output, output, b_new, h: int, intermediate: int, eps: float,
+                   threads: int = 256):
+    """output = silu(g * inv_rms + b_g) * (u * inv_rms + b_u) of a [gate | up]
+    GEMM output, through the C ABI."""
+    rc = lib().frn_rmsnorm_swiglu(
+        _dtype_code(x), x.data_ptr(), x.stride(0), raw_output.data_ptr(), raw_output.stride(0),
+        output.data_ptr(), output.stride(0), b_new.data_ptr(), x.shape[0], h, intermediate,
+        float(eps), int(threads), _stream_ptr(x.device))
+    check(rc, "frn_rmsnorm_swiglu")
+    return output
+
+
+def fused_rmsnorm_swiglu(x, w_combined, bias=None, eps: float = 1e-6, out=None):
+    """One-launch RMSNorm -> [gate | up] projection -> SwiGLU through the C ABI.
+
+    x: [M, K]; w_combined: [2I, K] (gate rows first); bias: [2I] or None;
+    returns out [M, I]."""
+    import torch
+
+    assert x.dim() == 2 and w_combined.dim() == 2 and x.stride(1) == 1
+    assert w_combined.stride(1) == 1 and w_combined.shape[0] % 2 == 0
+    M, K = x.shape
+    inter = w_combined.shape[0] // 2
+    if out is None:
+        out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
+    rc = lib().frn_fused_rmsnorm_swiglu(
+        _dtype_code(x), x.data_ptr(), M, K, x.stride(0), w_combined.data_ptr(), inter,
+        w_combined.stride(0), bias.data_ptr() if bias is not None else None, float(eps),
+        out.data_ptr(), out.stride(0), _stream_ptr(x.device))
+    check(rc, "frn_fused_rmsnorm_swiglu")
+    return out
 
 
 def device_error(device: int = 0, clear: bool = False) -> int:

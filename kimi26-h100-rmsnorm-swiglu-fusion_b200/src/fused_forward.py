@@ -55,6 +55,25 @@ def _fused_2d(x_2d: torch.Tensor, W: torch.Tensor, b: torch.Tensor, h: int, eps:
     return raw
 
 
+def _swiglu_2d(x_2d: torch.Tensor, W: torch.Tensor, b: torch.Tensor, intermediate: int, h: int,
+               eps: float, threads: int) -> torch.Tensor:
+    """[M, K] -> [M, I]: RMSNorm -> [gate | up] -> silu(gate) * up.  bf16/fp16 run
+    the single fused tcgen05 launch; fp32 runs F.linear and the reference's
+    rmsnorm_swiglu epilogue kernel (src/fused_forward.py:274-284 there)."""
+    if x_2d.size(-1) != h:
+        raise ValueError(f"x has {x_2d.size(-1)} features but the module was built for h={h}")
+    if W.size(0) != 2 * intermediate:
+        raise ValueError(f"W_combined has {W.size(0)} rows, expected 2*{intermediate}")
+    if x_2d.dtype in _TENSOR_CORE_DTYPES:
+        return denominator_cuda.fused_rmsnorm_swiglu(x_2d, W, b, float(eps))
+    raw = F.linear(x_2d, W)
+    out = torch.empty(x_2d.size(0), intermediate, dtype=x_2d.dtype, device=x_2d.device)
+    swiglu = (denominator_cuda.rmsnorm_swiglu_512 if threads == 512
+              else denominator_cuda.rmsnorm_swiglu)
+    swiglu(x_2d.contiguous(), raw, out, b, h, intermediate, float(eps))
+    return out
+
+
 def _apply(x: torch.Tensor, W: torch.Tensor, b: torch.Tensor, h: int, eps: float,
            threads: int) -> torch.Tensor:
     orig_shape = x.shape
@@ -147,10 +166,8 @@ class _FusedRMSNormSwiGLUBase(torch.nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         with _nvtx_range(self._range_name):
             batch_shape = x.shape[:-1]
-            gu = _fused_2d(x.reshape(-1, x.size(-1)), self.W_combined, self.b_combined, self.h,
-                           self.eps, self._threads)
-            gate, up = gu[:, : self.intermediate], gu[:, self.intermediate:]
-            out = F.silu(gate) * up
+            out = _swiglu_2d(x.reshape(-1, x.size(-1)), self.W_combined, self.b_combined,
+                             self.intermediate, self.h, self.eps, self._threads)
             return out.reshape(*batch_shape, self.intermediate)
 
 

@@ -15,6 +15,9 @@ unfused path or of its int8 quantization-aware path:
 * dequantize_int8         - src/benchmark_kimi26_quantized.py:38-39
 * fused_quantized         - src/benchmark_kimi26_quantized.py:102-106
 * fp32_truth / fp64_truth - the exact math the fused kernel approximates
+* swiglu_normalize_reference - csrc/denominator_kernel.cu:1286-1369 (rmsnorm_swiglu)
+* swiglu_module_reference - src/fused_forward.py:274-284 (FusedRMSNormSwiGLUV1.forward)
+* swiglu_unfused_reference - the model's silu(gate(norm(x))) * up(norm(x))
 
 The restatement is pinned against outputs of the reference itself, generated
 in the build container by tests/golden/make_golden.py and committed as
@@ -93,6 +96,47 @@ def normalize_inplace_reference(x: torch.Tensor, raw: torch.Tensor, b: torch.Ten
     (reference csrc/denominator_kernel.cu:1202-1273)."""
     r = inv_rms(x, eps)
     return (raw.float() * r[:, None] + b.float()).to(raw.dtype)
+
+
+# ------------------------------------------------------------- SwiGLU path
+
+
+def swiglu_normalize_reference(x: torch.Tensor, raw: torch.Tensor, b: torch.Tensor,
+                               intermediate: int, eps: float) -> torch.Tensor:
+    """What rmsnorm_swiglu(_512) writes from a [gate | up] GEMM output, fp32 math
+    and one rounding (reference csrc/denominator_kernel.cu:1286-1369):
+    g = raw[:, :I] * inv_rms + b[:I], u = raw[:, I:] * inv_rms + b[I:],
+    out = g / (1 + exp(-g)) * u."""
+    r = inv_rms(x, eps)[:, None]
+    rf, bf = raw.float(), b.float()
+    g = rf[:, :intermediate] * r + bf[:intermediate]
+    u = rf[:, intermediate:] * r + bf[intermediate:]
+    return (g / (1.0 + torch.exp(-g)) * u).to(raw.dtype)
+
+
+def swiglu_module_reference(x: torch.Tensor, W_combined: torch.Tensor, b: torch.Tensor,
+                            intermediate: int, eps: float) -> torch.Tensor:
+    """FusedRMSNormSwiGLUV1/V3.forward of the reference: F.linear(x,
+    W_combined) rounded to x's dtype, then rmsnorm_swiglu
+    (reference src/fused_forward.py:274-284)."""
+    return swiglu_normalize_reference(x, F.linear(x, W_combined), b, intermediate, eps)
+
+
+def swiglu_unfused_reference(x: torch.Tensor, gamma: torch.Tensor, W_gate: torch.Tensor,
+                             W_up: torch.Tensor, eps: float, norm: str = "torch") -> torch.Tensor:
+    """The model's own MLP input: silu(gate_proj(norm(x))) * up_proj(norm(x)) in
+    x's dtype (Llama's post_attention_layernorm -> act_fn(gate) * up)."""
+    y = simple_rmsnorm(x, gamma, eps) if norm == "simple" else torch_rmsnorm(x, gamma, eps)
+    return F.silu(F.linear(y, W_gate)) * F.linear(y, W_up)
+
+
+def swiglu_fp32_truth(x: torch.Tensor, W_combined: torch.Tensor, b: torch.Tensor | None,
+                      intermediate: int, eps: float) -> torch.Tensor:
+    """silu(inv_rms * x.Wg^T + b_g) * (inv_rms * x.Wu^T + b_u) in fp32: the fused
+    SwiGLU kernel's math before its single rounding."""
+    gu = fp32_truth(x, W_combined, b, eps)
+    g, u = gu[:, :intermediate], gu[:, intermediate:]
+    return g / (1.0 + torch.exp(-g)) * u
 
 
 # ----------------------------------------------------------------- int8 path
