@@ -207,9 +207,12 @@ int frn_fused_rmsnorm_swiglu(int dtype, const void* x, int64_t M, int64_t K,
   if (M == 0) return FRN_OK;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
-  const int pairs = sm_count(dev) / 2;
-  return run_fused_swiglu_pair(p, intermediate, choose_swiglu_bn(M, intermediate, K, pairs),
-                               static_cast<cudaStream_t>(stream));
+  const int sms = sm_count(dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M <= 128)
+    return run_fused_swiglu_decode(p, intermediate, choose_decode_split(2 * intermediate, K, sms),
+                                   s);
+  return run_fused_swiglu_pair(p, intermediate, choose_swiglu_bn(M, intermediate, K, sms / 2), s);
 }
 
 size_t frn_fused_rmsnorm_linear_workspace_size(int dtype, int64_t M, int64_t N, int64_t K) {

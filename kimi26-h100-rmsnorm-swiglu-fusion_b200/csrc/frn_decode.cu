@@ -17,6 +17,9 @@
 //             inv_rms[t] = rsqrt(sum_s ss_s[t] / K + eps) and b[n], and stores
 //             out[t, n0 .. n0+127] as coalesced rows.
 //
+// SwiGLU variant: a tile is 64 gate rows over the matching 64 up rows, and
+// the reduction combines the two halves into 64 output columns.
+//
 // Roles: warps 0-3 epilogue (TMEM lanes -> partial buffer) and reduction,
 // warps 4-7 TMA producers (W / x over even / odd stages), warp 8 MMA issuer +
 // TMEM owner, warps 9-12 RMS (thread t sums x[t, k-range]^2 from x stages).
@@ -38,6 +41,7 @@ struct DecodeParams {
   const void* bias;
   void* out;
   int64_t out_row_stride;
+  int32_t up_row0;  // SwiGLU: first W row of the up block (= intermediate)
   uint64_t timeout_ns;
 };
 
@@ -94,7 +98,10 @@ struct DecodeCfg {
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
-template <typename T, int MP, int STAGES>
+// SWIGLU: a W tile is 64 gate rows [g0, g0+64) over 64 up rows [I+g0, ...)
+// (two TMA boxes of 64 rows), and the reduction writes output columns
+// g0 + c = silu(D[c] * inv_rms + b[g0+c]) * (D[64+c] * inv_rms + b[I+g0+c]).
+template <typename T, int MP, int STAGES, bool SWIGLU>
 __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     fused_rmsnorm_linear_decode_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                        const __grid_constant__ CUtensorMap tmap_x,
@@ -117,7 +124,7 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   const int S = p.split;
   const uint32_t rank = cluster_cta_rank();
   const int tile = static_cast<int>(blockIdx.x) / S;
-  const int n0 = tile * C::BM;
+  const int n0 = tile * (SWIGLU ? C::BM / 2 : C::BM);  // first output column of the tile
   // k-blocks [kb_begin, kb_end) of this split (first splits take the remainder)
   const int base = p.num_k_blocks / S, rem = p.num_k_blocks % S;
   const int kb_begin = static_cast<int>(rank) * base + (static_cast<int>(rank) < rem ? rank : rem);
@@ -167,7 +174,13 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         const int kc = (kb_begin + i) * C::BK;
         if (is_w) {
           mbar_arrive_expect_tx(&full[stage], C::W_BYTES);
-          tma_load_2d(smem + C::OFF_W + stage * C::W_BYTES, &tmap_w, &full[stage], kc, n0);
+          uint8_t* wdst = smem + C::OFF_W + stage * C::W_BYTES;
+          if (SWIGLU) {
+            tma_load_2d(wdst, &tmap_w, &full[stage], kc, n0);
+            tma_load_2d(wdst + C::W_BYTES / 2, &tmap_w, &full[stage], kc, p.up_row0 + n0);
+          } else {
+            tma_load_2d(wdst, &tmap_w, &full[stage], kc, n0);
+          }
         } else {
           mbar_arrive_expect_tx(&full[stage], C::X_BYTES);
           tma_load_2d(smem + C::OFF_X + stage * C::X_BYTES, &tmap_x, &full[stage], kc, 0);
@@ -248,18 +261,28 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   cluster_sync_all();
 
   if (warp < 4 && !*abort_flag) {
-    // CTA `rank` reduces tokens rank, rank+S, ...: 64 threads per token, each
-    // owning W rows pr, pr+1 of the tile, two tokens in flight.
+    // CTA `rank` reduces tokens rank, rank+S, ...: TPT threads per token, each
+    // owning output columns pr, pr+1 of the tile (W rows pr, pr+1, and for
+    // SwiGLU also the up rows 64+pr, 65+pr); 128 / TPT tokens in flight.
     griddep_wait();
-    const int pr = static_cast<int>(threadIdx.x & 63u) * 2;
-    const int tsub = static_cast<int>(threadIdx.x >> 6);
+    constexpr int TPT = SWIGLU ? 32 : 64;
+    constexpr int LANES = 128 / TPT;
+    const int pr = static_cast<int>(threadIdx.x % TPT) * 2;
+    const int tsub = static_cast<int>(threadIdx.x / TPT);
+    const bool col_ok = n0 + pr < p.N;
     const bool has_bias = p.bias != nullptr;
-    float b0 = 0.f, b1 = 0.f;
-    if (has_bias && n0 + pr < p.N) {
-      const float2 bb = pair_to_float2<T>(*reinterpret_cast<const uint32_t*>(
-          static_cast<const T*>(p.bias) + n0 + pr));
+    float b0 = 0.f, b1 = 0.f, bu0 = 0.f, bu1 = 0.f;
+    if (has_bias && col_ok) {
+      const T* bias = static_cast<const T*>(p.bias);
+      const float2 bb = pair_to_float2<T>(*reinterpret_cast<const uint32_t*>(bias + n0 + pr));
       b0 = bb.x;
       b1 = bb.y;
+      if (SWIGLU) {
+        const float2 bv = pair_to_float2<T>(
+            *reinterpret_cast<const uint32_t*>(bias + p.up_row0 + n0 + pr));
+        bu0 = bv.x;
+        bu1 = bv.y;
+      }
     }
     const uint32_t part_local = smem_addr(part);
     const uint32_t ssq_local = smem_addr(ssq);
@@ -268,37 +291,51 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     constexpr int kBatch = 4;
     const int t_first = static_cast<int>(rank) + S * tsub;
     const int t_end = p.M < MP ? p.M : MP;
-    for (int t0 = t_first; t0 < t_end; t0 += 2 * S * kBatch) {
-      float2 acc[kBatch];
+    for (int t0 = t_first; t0 < t_end; t0 += LANES * S * kBatch) {
+      float2 acc[kBatch], accu[kBatch];
       float ss[kBatch];
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j) { acc[j] = make_float2(0.f, 0.f); ss[j] = 0.f; }
+      for (int j = 0; j < kBatch; ++j) {
+        acc[j] = make_float2(0.f, 0.f);
+        accu[j] = make_float2(0.f, 0.f);
+        ss[j] = 0.f;
+      }
       for (int s = 0; s < S; ++s) {  // fixed rank order: deterministic sums
         const uint32_t part_s = mapa_shared(part_local, s);
         const uint32_t ssq_s = mapa_shared(ssq_local, s);
-        float2 v[kBatch];
+        float2 v[kBatch], u[kBatch];
         float q[kBatch];
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-          const int t = t0 + j * 2 * S;
+          const int t = t0 + j * LANES * S;
           const int tc = t < t_end ? t : t_first;  // clamp: loads stay in bounds
           v[j] = ld_shared_cluster_f32x2(part_s + (tc * C::BM + pr) * 4);
+          if (SWIGLU) u[j] = ld_shared_cluster_f32x2(part_s + (tc * C::BM + 64 + pr) * 4);
           q[j] = ld_shared_cluster_f32(ssq_s + tc * 4);
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
           acc[j].x += v[j].x;
           acc[j].y += v[j].y;
+          if (SWIGLU) {
+            accu[j].x += u[j].x;
+            accu[j].y += u[j].y;
+          }
           ss[j] += q[j];
         }
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        const int t = t0 + j * 2 * S;
-        if (t < t_end && n0 + pr < p.N) {
+        const int t = t0 + j * LANES * S;
+        if (t < t_end && col_ok) {
           const float r = rsqrtf(ss[j] / static_cast<float>(p.K) + p.eps);
           T* o = static_cast<T*>(p.out) + static_cast<int64_t>(t) * p.out_row_stride + n0 + pr;
-          *reinterpret_cast<uint32_t*>(o) = float2_to_pair<T>(acc[j].x * r + b0, acc[j].y * r + b1);
+          float y0 = acc[j].x * r + b0, y1 = acc[j].y * r + b1;
+          if (SWIGLU) {
+            y0 = __fdividef(y0, 1.0f + __expf(-y0)) * (accu[j].x * r + bu0);
+            y1 = __fdividef(y1, 1.0f + __expf(-y1)) * (accu[j].y * r + bu1);
+          }
+          *reinterpret_cast<uint32_t*>(o) = float2_to_pair<T>(y0, y1);
         }
       }
     }
@@ -319,7 +356,7 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
 // ------------------------------------------------------------------ host side
 
 // Clusters of `split` CTAs of this kernel that can be resident at once.
-template <typename T, int MP, int STAGES>
+template <typename T, int MP, int STAGES, bool SWIGLU>
 static int max_clusters(int split) {
   using C = DecodeCfg<MP, STAGES>;
   cudaLaunchConfig_t qc = {};
@@ -334,7 +371,8 @@ static int max_clusters(int split) {
   qc.attrs = qa;
   qc.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, fused_rmsnorm_linear_decode_kernel<T, MP, STAGES>, &qc) !=
+  if (cudaOccupancyMaxActiveClusters(&n, fused_rmsnorm_linear_decode_kernel<T, MP, STAGES, SWIGLU>,
+                                     &qc) !=
       cudaSuccess) {
     cudaGetLastError();
     return 0;
@@ -342,10 +380,16 @@ static int max_clusters(int split) {
   return n;
 }
 
-template <typename T, int MP, int STAGES>
-static int launch_decode(const LinearProblem& pr, int split, cudaStream_t stream) {
+// SWIGLU: pr.w = [gate; up] (pr.N = 2 * inter rows); the output has `inter`
+// columns, 64 per tile.
+template <typename T, int MP, int STAGES, bool SWIGLU = false>
+static int launch_decode(const LinearProblem& pr, int split, cudaStream_t stream,
+                         int64_t inter = 0) {
   using C = DecodeCfg<MP, STAGES>;
-  auto kern = fused_rmsnorm_linear_decode_kernel<T, MP, STAGES>;
+  auto kern = fused_rmsnorm_linear_decode_kernel<T, MP, STAGES, SWIGLU>;
+  const int64_t n_out = SWIGLU ? inter : pr.N;
+  const int tile_cols = SWIGLU ? C::BM / 2 : C::BM;
+  const int tiles = static_cast<int>((n_out + tile_cols - 1) / tile_cols);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
   static bool attr_set[kMaxDevices] = {};
@@ -361,25 +405,24 @@ static int launch_decode(const LinearProblem& pr, int split, cudaStream_t stream
   // wave: a second wave would double the time of this weight stream.
   {
     static int fits[kMaxDevices][9] = {};
-    const int64_t tiles64 = (pr.N + C::BM - 1) / C::BM;
     while (split > 1) {
       int& f = fits[dev < kMaxDevices ? dev : 0][split];
-      if (f == 0) f = max_clusters<T, MP, STAGES>(split) + 1;  // +1: 0 means "not queried"
-      if (tiles64 <= f - 1) break;
+      if (f == 0) f = max_clusters<T, MP, STAGES, SWIGLU>(split) + 1;  // 0 = "not queried"
+      if (tiles <= f - 1) break;
       --split;
     }
   }
   const CUtensorMapDataType dt = Elem16<T>::kTmaType;
   CUtensorMap tw, tx;
-  int rc = encode_tmap_2d(&tw, dt, 2, pr.w, pr.K, pr.N, pr.w_row_stride, C::BK, C::BM,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = encode_tmap_2d(&tw, dt, 2, pr.w, pr.K, pr.N, pr.w_row_stride, C::BK,
+                          SWIGLU ? C::BM / 2 : C::BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = encode_tmap_2d(&tx, dt, 2, pr.x, pr.K, pr.M, pr.x_row_stride, C::BK, MP,
                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   DecodeParams p;
   p.M = static_cast<int32_t>(pr.M);
-  p.N = static_cast<int32_t>(pr.N);
+  p.N = static_cast<int32_t>(n_out);
   p.K = static_cast<int32_t>(pr.K);
   p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
   p.split = split;
@@ -387,8 +430,8 @@ static int launch_decode(const LinearProblem& pr, int split, cudaStream_t stream
   p.bias = pr.bias;
   p.out = pr.out;
   p.out_row_stride = pr.out_row_stride;
+  p.up_row0 = static_cast<int32_t>(inter);
   p.timeout_ns = wait_timeout_ns();
-  const int tiles = static_cast<int>((pr.N + C::BM - 1) / C::BM);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles * split);
@@ -434,6 +477,23 @@ int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s) 
   if (pr.dtype == FRN_DTYPE_BF16) return run_decode_t<__nv_bfloat16>(pr, split, s);
   if (pr.dtype == FRN_DTYPE_F16) return run_decode_t<__half>(pr, split, s);
   return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+Linear supports bf16 and fp16 only");
+}
+
+template <typename T>
+static int run_decode_swiglu_t(const LinearProblem& pr, int64_t inter, int split,
+                               cudaStream_t s) {
+  if (pr.M <= 16) return launch_decode<T, 16, 8, true>(pr, split, s, inter);
+  if (pr.M <= 32) return launch_decode<T, 32, 8, true>(pr, split, s, inter);
+  if (pr.M <= 64) return launch_decode<T, 64, 6, true>(pr, split, s, inter);
+  if (pr.M <= 128) return launch_decode<T, 128, 6, true>(pr, split, s, inter);
+  return set_error(FRN_ERR_UNSUPPORTED, "decode kernel takes M <= 128 (got %lld)",
+                   static_cast<long long>(pr.M));
+}
+
+int run_fused_swiglu_decode(const LinearProblem& pr, int64_t inter, int split, cudaStream_t s) {
+  if (pr.dtype == FRN_DTYPE_BF16) return run_decode_swiglu_t<__nv_bfloat16>(pr, inter, split, s);
+  if (pr.dtype == FRN_DTYPE_F16) return run_decode_swiglu_t<__half>(pr, inter, split, s);
+  return set_error(FRN_ERR_UNSUPPORTED, "fused RMSNorm+SwiGLU supports bf16 and fp16 only");
 }
 
 }  // namespace frn

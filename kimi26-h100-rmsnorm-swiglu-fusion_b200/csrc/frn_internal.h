@@ -76,6 +76,7 @@ int run_fused_swiglu_pair(const LinearProblem& pr, int64_t inter, int bn, cudaSt
 // Decode (M <= 128) swap-AB kernel, `split` CTAs per cluster along K.
 int choose_decode_split(int64_t N, int64_t K, int sms);
 int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s);
+int run_fused_swiglu_decode(const LinearProblem& pr, int64_t inter, int split, cudaStream_t s);
 
 int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s);
 int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws, void* q,

@@ -110,6 +110,27 @@ def test_fused_swiglu_llama_mlp_prefill():
     assert capi.device_error(0) == 0
 
 
+@pytest.mark.parametrize("M", [1, 8, 32, 64, 128])
+def test_fused_swiglu_decode_path(M):
+    """M <= 128 takes the swap-AB split-K decode kernel (64 gate rows over the
+    matching 64 up rows per W tile)."""
+    K, inter = 4096, 1984
+    x, gamma, W, Wc, b = _inputs(M, K, inter, seed=M, bias=(M == 32))
+    out = capi.fused_rmsnorm_swiglu(x.to(DEV), Wc.to(DEV), b.to(DEV) if M == 32 else None,
+                                    orc.EPS)
+    torch.cuda.synchronize()
+    _check_fused(out, x, gamma, W, Wc, b, inter, f"decode M={M}", has_bias=(M == 32))
+
+
+def test_fused_swiglu_llama_mlp_decode():
+    """Llama-3-8B MLP gate/up (K=4096, I=14336) at a decode batch of 8."""
+    M, K, inter = 8, 4096, 14336
+    x, gamma, W, Wc, b = _inputs(M, K, inter, seed=88)
+    out = capi.fused_rmsnorm_swiglu(x.to(DEV), Wc.to(DEV), None, orc.EPS)
+    torch.cuda.synchronize()
+    _check_fused(out, x, gamma, W, Wc, b, inter, "llama mlp decode", has_bias=False)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("threads", [256, 512])
 def test_rmsnorm_swiglu_epilogue(dtype, threads):
