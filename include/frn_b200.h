@@ -156,6 +156,21 @@ int frn_quantize_int8_per_channel(int dtype, const void* w, int64_t N, int64_t K
                                   float* scale, void* stream);
 
 /*
+ * frn_fused_rmsnorm_linear with the output columns written straight into
+ * `nparts` (1..4) separate tensors: part i takes the next part_cols[i]
+ * columns (a positive multiple of 8; of 64 when M > 128) and is stored at
+ * part_out[i] with row stride part_row_stride[i] elements.  The widths sum to
+ * N.  Replaces FusedRMSNormCombinedLinearV1/V3.forward's split + per-part
+ * .contiguous() copies (reference src/fused_forward.py:194-251, :222-224).
+ */
+#define FRN_MAX_PARTS 4
+int frn_fused_rmsnorm_linear_split(int dtype, const void* x, int64_t M, int64_t K,
+                                   int64_t x_row_stride, const void* w, int64_t N,
+                                   int64_t w_row_stride, const void* bias, float eps, int nparts,
+                                   const int64_t* part_cols, void* const* part_out,
+                                   const int64_t* part_row_stride, void* stream);
+
+/*
  * RMSNorm + SwiGLU epilogue of a precomputed [gate | up] GEMM output
  * raw_output[rows, 2*intermediate] (raw = x . W_combined^T):
  *     g = raw[r, c] * inv_rms[r] + b_new[c]

@@ -70,6 +70,48 @@ void rmsnorm_normalize_512(const at::Tensor& x, at::Tensor raw_output, const at:
   rmsnorm_normalize_impl(x, raw_output, b_new, h, eps, 512, "rmsnorm_normalize_512");
 }
 
+std::vector<at::Tensor> fused_rmsnorm_linear_split(const at::Tensor& x_in, const at::Tensor& w,
+                                                   const c10::optional<at::Tensor>& b_new,
+                                                   double eps, std::vector<int64_t> split_sizes) {
+  TORCH_CHECK(x_in.dim() == 2 && w.dim() == 2, "x and W_fused must be 2D");
+  TORCH_CHECK(x_in.is_cuda() && w.is_cuda() && (!b_new || b_new->is_cuda()),
+              "All tensors must be on CUDA");
+  TORCH_CHECK(x_in.scalar_type() == at::kBFloat16 || x_in.scalar_type() == at::kHalf,
+              "fused_rmsnorm_linear_split supports bf16 and fp16 (got ", x_in.scalar_type(), ")");
+  TORCH_CHECK(w.scalar_type() == x_in.scalar_type(), "x and W_fused must share one dtype");
+  TORCH_CHECK(x_in.size(1) == w.size(1), "x.size(1) != W_fused.size(1)");
+  const int n = static_cast<int>(split_sizes.size());
+  TORCH_CHECK(n >= 1 && n <= FRN_MAX_PARTS, "split_sizes must have 1..", FRN_MAX_PARTS,
+              " entries");
+  const at::Tensor x = (x_in.stride(1) == 1 || x_in.size(1) == 1) ? x_in : x_in.contiguous();
+  const at::Tensor wc = (w.stride(1) == 1) ? w : w.contiguous();
+  const int64_t M = x.size(0), K = x.size(1), N = wc.size(0);
+  at::Tensor b;
+  const void* bptr = nullptr;
+  if (b_new && b_new->defined()) {
+    TORCH_CHECK(b_new->numel() == N && b_new->scalar_type() == x.scalar_type(),
+                "b_new must have W_fused.size(0) elements of x's dtype");
+    b = b_new->contiguous();
+    bptr = b.data_ptr();
+  }
+  std::vector<at::Tensor> outs;
+  int64_t cols[FRN_MAX_PARTS], strides[FRN_MAX_PARTS];
+  void* ptrs[FRN_MAX_PARTS];
+  for (int i = 0; i < n; ++i) {
+    outs.push_back(at::empty({M, split_sizes[i]}, x.options()));
+    cols[i] = split_sizes[i];
+    strides[i] = outs.back().stride(0);
+    ptrs[i] = outs.back().data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  check_rc(frn_fused_rmsnorm_linear_split(dtype_code(x), x.data_ptr(), M, K, x.stride(0),
+                                          wc.data_ptr(), N, wc.stride(0), bptr,
+                                          static_cast<float>(eps), n, cols, ptrs, strides,
+                                          stream_of(x)),
+           "fused_rmsnorm_linear_split");
+  return outs;
+}
+
 void rmsnorm_swiglu_impl(const at::Tensor& x, const at::Tensor& raw_output, at::Tensor& output,
                          const at::Tensor& b_new, int64_t h, int64_t intermediate, double eps,
                          int threads, const char* name) {
@@ -292,6 +334,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_normalize_512", &rmsnorm_normalize_512,
         "In-place RMSNorm rescale of a GEMM output (512 threads per row)", py::arg("x"),
         py::arg("raw_output"), py::arg("b_new"), py::arg("h"), py::arg("eps"));
+  m.def("fused_rmsnorm_linear_split", &fused_rmsnorm_linear_split,
+        "fused_rmsnorm_linear whose output columns are written into separate [M, n_i] tensors",
+        py::arg("x"), py::arg("W_fused"), py::arg("b_new"), py::arg("eps"),
+        py::arg("split_sizes"));
   m.def("rmsnorm_swiglu", &rmsnorm_swiglu,
         "RMSNorm + SwiGLU of a [gate | up] GEMM output into output (256 threads per row)",
         py::arg("x"), py::arg("raw_output"), py::arg("output"), py::arg("b_new"), py::arg("h"),

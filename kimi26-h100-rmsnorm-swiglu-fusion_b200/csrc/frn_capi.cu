@@ -256,6 +256,60 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
   return set_error(FRN_ERR_UNSUPPORTED, "kernel id %d not available", kernel);
 }
 
+int frn_fused_rmsnorm_linear_split(int dtype, const void* x, int64_t M, int64_t K,
+                                   int64_t x_row_stride, const void* w, int64_t N,
+                                   int64_t w_row_stride, const void* bias, float eps, int nparts,
+                                   const int64_t* part_cols, void* const* part_out,
+                                   const int64_t* part_row_stride, void* stream) {
+  if (nparts < 1 || nparts > kMaxParts)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "nparts must be 1..%d (got %d)", kMaxParts,
+                     nparts);
+  if (!part_cols || !part_out || !part_row_stride)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "part arrays must be non-null");
+  OutParts parts;
+  parts.n = nparts;
+  int64_t c0 = 0;
+  bool all64 = true;
+  for (int i = 0; i < nparts; ++i) {
+    if (part_cols[i] <= 0 || part_cols[i] % 8)
+      return set_error(FRN_ERR_MISALIGNED, "part %d width %lld must be a positive multiple of 8",
+                       i, (long long)part_cols[i]);
+    if (part_row_stride[i] < part_cols[i] || part_row_stride[i] % 8)
+      return set_error(FRN_ERR_MISALIGNED,
+                       "part %d row stride %lld must be >= its width and a multiple of 8", i,
+                       (long long)part_row_stride[i]);
+    if (M > 0 && (!part_out[i] || !aligned16(part_out[i])))
+      return set_error(FRN_ERR_MISALIGNED, "part %d output must be non-null and 16-byte aligned",
+                       i);
+    all64 = all64 && (part_cols[i] % 64 == 0);
+    parts.col0[i] = c0;
+    parts.cols[i] = part_cols[i];
+    parts.out[i] = part_out[i];
+    parts.stride[i] = part_row_stride[i];
+    c0 += part_cols[i];
+  }
+  if (c0 != N)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "part widths sum to %lld, N is %lld",
+                     (long long)c0, (long long)N);
+  // Validated as a plain [M, N] linear (the first part stands in for out).
+  LinearProblem p{dtype, x, M, K, x_row_stride, w, N, w_row_stride, bias, eps,
+                  part_out[0], N, nullptr, 0};
+  int rc = validate_linear(p);
+  if (rc) return rc;
+  p.out_row_stride = part_row_stride[0];
+  p.parts = &parts;
+  if (M == 0) return FRN_OK;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int sms = sm_count(dev);
+  if (M <= 128) return run_fused_linear_decode(p, choose_decode_split(N, K, sms), s);
+  if (!all64 && nparts > 1)
+    return set_error(FRN_ERR_UNSUPPORTED,
+                     "for M > 128 the split parts must be multiples of 64 columns");
+  return run_fused_linear_pair(p, choose_pair_tiling(M, N, K, sms / 2, nparts > 1), s);
+}
+
 int frn_fused_rmsnorm_linear(int dtype, const void* x, int64_t M, int64_t K, int64_t x_row_stride,
                              const void* w, int64_t N, int64_t w_row_stride, const void* bias,
                              float eps, void* out, int64_t out_row_stride, void* workspace,

@@ -39,8 +39,12 @@ struct DecodeParams {
   int32_t split;  // CTAs per cluster (k-splits)
   float eps;
   const void* bias;
-  void* out;
-  int64_t out_row_stride;
+  // Output parts: columns [part_col0[i], part_col0[i+1]) go to part_out[i]
+  // (row stride part_stride[i]); one part is the plain [M, N] output.
+  int32_t nparts;
+  int32_t part_col0[kMaxParts];
+  void* part_out[kMaxParts];
+  int64_t part_stride[kMaxParts];
   int32_t up_row0;  // SwiGLU: first W row of the up block (= intermediate)
   uint64_t timeout_ns;
 };
@@ -270,6 +274,10 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     const int pr = static_cast<int>(threadIdx.x % TPT) * 2;
     const int tsub = static_cast<int>(threadIdx.x / TPT);
     const bool col_ok = n0 + pr < p.N;
+    int pi = 0;  // output part of columns n0 + pr, n0 + pr + 1 (parts are 8-column multiples)
+    while (pi + 1 < p.nparts && n0 + pr >= p.part_col0[pi + 1]) ++pi;
+    T* const obase = static_cast<T*>(p.part_out[pi]) + (n0 + pr - p.part_col0[pi]);
+    const int64_t ostride = p.part_stride[pi];
     const bool has_bias = p.bias != nullptr;
     float b0 = 0.f, b1 = 0.f, bu0 = 0.f, bu1 = 0.f;
     if (has_bias && col_ok) {
@@ -329,7 +337,7 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         const int t = t0 + j * LANES * S;
         if (t < t_end && col_ok) {
           const float r = rsqrtf(ss[j] / static_cast<float>(p.K) + p.eps);
-          T* o = static_cast<T*>(p.out) + static_cast<int64_t>(t) * p.out_row_stride + n0 + pr;
+          T* o = obase + static_cast<int64_t>(t) * ostride;
           float y0 = acc[j].x * r + b0, y1 = acc[j].y * r + b1;
           if (SWIGLU) {
             y0 = __fdividef(y0, 1.0f + __expf(-y0)) * (accu[j].x * r + bu0);
@@ -428,8 +436,22 @@ static int launch_decode(const LinearProblem& pr, int split, cudaStream_t stream
   p.split = split;
   p.eps = pr.eps;
   p.bias = pr.bias;
-  p.out = pr.out;
-  p.out_row_stride = pr.out_row_stride;
+  if (pr.parts && pr.parts->n > 1) {
+    p.nparts = pr.parts->n;
+    for (int i = 0; i < kMaxParts; ++i) {
+      const bool used = i < pr.parts->n;
+      p.part_col0[i] = used ? static_cast<int32_t>(pr.parts->col0[i]) : 0x7fffffff;
+      p.part_out[i] = used ? pr.parts->out[i] : nullptr;
+      p.part_stride[i] = used ? pr.parts->stride[i] : 0;
+    }
+  } else {
+    p.nparts = 1;
+    for (int i = 0; i < kMaxParts; ++i) {
+      p.part_col0[i] = i == 0 ? 0 : 0x7fffffff;
+      p.part_out[i] = i == 0 ? pr.out : nullptr;
+      p.part_stride[i] = i == 0 ? pr.out_row_stride : 0;
+    }
+  }
   p.up_row0 = static_cast<int32_t>(inter);
   p.timeout_ns = wait_timeout_ns();
 

@@ -36,6 +36,16 @@
 
 namespace frn {
 
+// Output tensor maps: [32 rows x 64 columns] store boxes (128B swizzle), one
+// per output part, plus a [32 x 32] box (64B swizzle) for tiles whose last
+// chunk is 32 columns wide (single output only).
+struct PairOut {
+  CUtensorMap map[kMaxParts];
+  CUtensorMap half;
+  int32_t col0[kMaxParts];  // first output column of each part
+  int32_t nparts;
+};
+
 struct PairParams {
   int32_t M, N, K;
   int32_t num_m_blocks;  // of 256 rows
@@ -97,8 +107,7 @@ template <typename T, int BN, int STAGES, int NACC, bool SWIGLU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, NACC>::THREADS, 1)
     fused_rmsnorm_linear_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                      const __grid_constant__ CUtensorMap tmap_w,
-                                     const __grid_constant__ CUtensorMap tmap_out,
-                                     const __grid_constant__ CUtensorMap tmap_out_half,
+                                     const __grid_constant__ PairOut outm,
                                      const PairParams p) {
   using C = PairCfg<BN, STAGES, NACC>;
   static_assert(!SWIGLU || NACC == 2, "the SwiGLU epilogue pairs the two accumulators");
@@ -128,8 +137,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
   if (warp == C::WARP_PROD0 && lane == 0) {
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_w);
-    prefetch_tmap(&tmap_out);
-    if (OUT_N % 64 != 0) prefetch_tmap(&tmap_out_half);
+    for (int i = 0; i < outm.nparts; ++i) prefetch_tmap(&outm.map[i]);
+    if (OUT_N % 64 != 0) prefetch_tmap(&outm.half);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&mma_done[s], 1);
@@ -361,7 +370,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(half ? &tmap_out_half : &tmap_out, sbp, col0, row_base);
+            tma_store_2d(half ? &outm.half : &outm.map[0], sbp, col0, row_base);
             bulk_commit_group();
           }
         }
@@ -411,7 +420,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(half ? &tmap_out_half : &tmap_out, sbp, col0, row_base);
+          // Part of this chunk (a chunk never straddles two parts: split
+          // outputs take 64-column multiples for parts and tiles).
+          int pi = 0;
+          while (pi + 1 < outm.nparts && col0 >= outm.col0[pi + 1]) ++pi;
+          tma_store_2d(half ? &outm.half : &outm.map[pi], sbp, col0 - outm.col0[pi], row_base);
           bulk_commit_group();
         }
       }
@@ -486,16 +499,35 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream, int64_t int
   if (rc) return rc;
   // Output: one warp's [32 rows x 64 columns] block per store (128B swizzle),
   // and [32 x 32] with the 64B swizzle for a tile whose last chunk is 32 wide.
-  CUtensorMap to, toh;
-  rc = encode_tmap_2d(&to, dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 64, 32,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  if (OUT_N % 64 != 0) {
-    rc = encode_tmap_2d(&toh, dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 32, 32,
-                        CU_TENSOR_MAP_SWIZZLE_64B);
-    if (rc) return rc;
+  PairOut outm;
+  if (pr.parts && pr.parts->n > 1) {
+    if (SWIGLU || OUT_N % 64 != 0)
+      return set_error(FRN_ERR_UNSUPPORTED, "split output needs a tile width multiple of 64");
+    outm.nparts = pr.parts->n;
+    for (int i = 0; i < pr.parts->n; ++i) {
+      rc = encode_tmap_2d(&outm.map[i], dt, 2, pr.parts->out[i], pr.parts->cols[i], pr.M,
+                          pr.parts->stride[i], 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (rc) return rc;
+      outm.col0[i] = static_cast<int32_t>(pr.parts->col0[i]);
+    }
+    outm.half = outm.map[0];
   } else {
-    toh = to;
+    outm.nparts = 1;
+    outm.col0[0] = 0;
+    rc = encode_tmap_2d(&outm.map[0], dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 64, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (OUT_N % 64 != 0) {
+      rc = encode_tmap_2d(&outm.half, dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 32, 32,
+                          CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc) return rc;
+    } else {
+      outm.half = outm.map[0];
+    }
+  }
+  for (int i = outm.nparts; i < kMaxParts; ++i) {
+    outm.map[i] = outm.map[0];
+    outm.col0[i] = 0x7fffffff;
   }
 
   PairParams p;
@@ -524,7 +556,7 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream, int64_t int
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, to, toh, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tw, outm, p);
   if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_pair", e);
   return 0;
 }
@@ -538,7 +570,7 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream, int64_t int
 // A tile costs max(mma, feed); with NACC = 1 the epilogue overlaps the next
 // tile and only the last one is exposed, with NACC = 2 every epilogue is.
 // The busiest pair runs ceil(tiles / pairs) tiles.
-PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs) {
+PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs, bool tile64) {
   const double mb = static_cast<double>((M + 255) / 256);
   const double nkb = static_cast<double>((K + 63) / 64);
   static const PairChoice cands[] = {{256, 1}, {224, 1}, {192, 1}, {160, 1}, {128, 1},
@@ -546,6 +578,7 @@ PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs) {
   double best = 1e300;
   PairChoice pick = {256, 1};
   for (const PairChoice& c : cands) {
+    if (tile64 && (c.nacc * c.bn) % 64 != 0) continue;
     const double tn = static_cast<double>(c.nacc * c.bn);
     const double tiles = mb * std::ceil(static_cast<double>(N) / tn);
     const double per_pair = std::ceil(tiles / pairs);

@@ -16,6 +16,18 @@ constexpr int kMaxDevices = 64;
 
 // One fused RMSNorm -> Linear problem, validated by the C ABI before any
 // launcher sees it.  Strides are in elements.
+// Output columns [0, N) split into up to kMaxParts separate tensors: part p
+// holds columns [col0[p], col0[p] + cols[p]) at out[p] with row stride
+// stride[p] (elements).  One part = the plain [M, N] output.
+constexpr int kMaxParts = 4;
+struct OutParts {
+  int n;
+  int64_t col0[kMaxParts];
+  int64_t cols[kMaxParts];
+  void* out[kMaxParts];
+  int64_t stride[kMaxParts];
+};
+
 struct LinearProblem {
   int dtype;
   const void* x;
@@ -28,6 +40,7 @@ struct LinearProblem {
   int64_t out_row_stride;
   void* workspace;
   size_t workspace_bytes;
+  const OutParts* parts = nullptr;  // non-null: write the split parts instead of out
 };
 
 // One int8-weight problem (strides in elements; wq_row_stride in bytes).
@@ -67,7 +80,9 @@ struct PairChoice {
   int bn;
   int nacc;
 };
-PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs);
+// tile64: only tilings whose output tile width is a multiple of 64 columns
+// (split outputs store whole 64-column chunks per part).
+PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs, bool tile64 = false);
 int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s);
 // SwiGLU on the pair kernel: pr.w = [gate; up] with pr.N = 2 * inter rows;
 // the output has `inter` columns; tiles are 256 x bn output columns.

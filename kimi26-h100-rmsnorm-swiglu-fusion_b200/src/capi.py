@@ -70,6 +70,12 @@ PROTOTYPES = {
         c_int,
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
     ),
+    "frn_fused_rmsnorm_linear_split": (
+        c_int,
+        [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+         c_float, c_int, ctypes.POINTER(c_int64), ctypes.POINTER(c_void_p),
+         ctypes.POINTER(c_int64), c_void_p],
+    ),
     "frn_rmsnorm_swiglu": (
         c_int,
         [c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
@@ -197,6 +203,28 @@ def quantize_int8_per_channel(w):
                                              _stream_ptr(w.device))
     check(rc, "frn_quantize_int8_per_channel")
     return q, scale
+
+
+def fused_rmsnorm_linear_split(x, w, bias, eps: float, split_sizes, outs=None):
+    """Fused RMSNorm -> Linear whose output columns land directly in
+    len(split_sizes) separate [M, n_i] tensors (returned as a list)."""
+    import torch
+
+    assert x.dim() == 2 and w.dim() == 2 and x.stride(1) == 1 and w.stride(1) == 1
+    M, K = x.shape
+    N = w.shape[0]
+    n = len(split_sizes)
+    if outs is None:
+        outs = [torch.empty(M, c, dtype=x.dtype, device=x.device) for c in split_sizes]
+    cols = (c_int64 * n)(*[int(c) for c in split_sizes])
+    ptrs = (c_void_p * n)(*[o.data_ptr() for o in outs])
+    strides = (c_int64 * n)(*[o.stride(0) for o in outs])
+    rc = lib().frn_fused_rmsnorm_linear_split(
+        _dtype_code(x), x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0),
+        bias.data_ptr() if bias is not None else None, float(eps), n, cols, ptrs, strides,
+        _stream_ptr(x.device))
+    check(rc, "frn_fused_rmsnorm_linear_split")
+    return outs
 
 
 def rmsnorm_swiglu(x, raw_output, output, b_new, h: int, intermediate: int, eps: float,

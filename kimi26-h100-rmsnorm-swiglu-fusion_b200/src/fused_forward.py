@@ -131,10 +131,28 @@ class _FusedRMSNormCombinedBase(torch.nn.Module):
     def forward(self, x: torch.Tensor) -> list[torch.Tensor]:
         with _nvtx_range(self._range_name):
             batch_shape = x.shape[:-1]
-            out = _fused_2d(x.reshape(-1, x.size(-1)), self.W_combined, self.b_combined,
-                            self.h, self.eps, self._threads)
+            x_2d = x.reshape(-1, x.size(-1))
+            if x_2d.size(-1) != self.h:
+                raise ValueError(f"x has {x_2d.size(-1)} features but the module was built "
+                                 f"for h={self.h}")
+            if x_2d.dtype in _TENSOR_CORE_DTYPES and self._split_ok(x_2d.size(0)):
+                # One launch writes every part straight into its own tensor.
+                parts = denominator_cuda.fused_rmsnorm_linear_split(
+                    x_2d, self.W_combined, self.b_combined, float(self.eps),
+                    list(self.split_sizes))
+                return [p.reshape(*batch_shape, p.size(-1)) for p in parts]
+            out = _fused_2d(x_2d, self.W_combined, self.b_combined, self.h, self.eps,
+                            self._threads)
             parts = torch.split(out, self.split_sizes, dim=-1)
             return [p.contiguous().reshape(*batch_shape, p.size(-1)) for p in parts]
+
+    def _split_ok(self, m: int) -> bool:
+        """Direct split output: at most 4 parts of 8-column multiples, and of
+        64-column multiples once the token count leaves the decode kernel."""
+        sizes = list(self.split_sizes)
+        if not 1 <= len(sizes) <= 4 or any(c % 8 for c in sizes):
+            return False
+        return m <= 128 or all(c % 64 == 0 for c in sizes)
 
 
 class FusedRMSNormCombinedLinearV1(_FusedRMSNormCombinedBase):
