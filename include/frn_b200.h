@@ -206,6 +206,26 @@ int frn_fused_rmsnorm_swiglu(int dtype, const void* x, int64_t M, int64_t K,
                              int64_t out_row_stride, void* stream);
 
 /*
+ * Decode-step grouped-query attention (one query token per sequence):
+ *     out[b, h, :] = softmax_t(scale * q[b, h, :] . K[b, t, h/G, :]) @ V[b, :, h/G, :]
+ * q [batch, num_q_heads, head_dim], k_cache / v_cache [batch, context_len,
+ * num_kv_heads, head_dim], out [batch, num_q_heads, head_dim], all contiguous
+ * and of `dtype` (fp32 / fp16 / bf16); head_dim 64 or 128; G = num_q_heads /
+ * num_kv_heads <= 8.  The context is split across CTAs when `workspace`
+ * (frn_gqa_decode_workspace_size bytes) is given; with no workspace each
+ * (batch, KV head) is one CTA.  Replaces gqa_decode_v2_cuda / gqa_decode_v3_cuda
+ * (reference csrc/gqa_attention_kernel.cu:357-470, bound in
+ * csrc/gqa_attention.cpp:45-60), on the caller's stream.
+ */
+size_t frn_gqa_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                     int64_t head_dim, int64_t context_len);
+int frn_gqa_decode_attention(int dtype, const void* q, const void* k_cache, const void* v_cache,
+                             void* out, int64_t batch, int64_t num_q_heads,
+                             int64_t num_kv_heads, int64_t head_dim, int64_t context_len,
+                             float scale, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/*
  * Reads (and optionally clears) the device error word of `device`, which
  * kernels set when a bounded wait expires instead of hanging.  Synchronous
  * with respect to the device's legacy default stream.

@@ -112,6 +112,46 @@ std::vector<at::Tensor> fused_rmsnorm_linear_split(const at::Tensor& x_in, const
   return outs;
 }
 
+// ---- decode-step GQA attention (gqa_attention_cuda exports of the reference)
+void gqa_decode_impl(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                     at::Tensor& out, double scale, const char* name) {
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 4 && v.dim() == 4 && out.dim() == 3,
+              name, ": q/out must be [batch, heads, head_dim], caches [batch, ctx, kv_heads, head_dim]");
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda() && out.is_cuda(),
+              "All tensors must be on CUDA");
+  const int dt = dtype_code(q);
+  TORCH_CHECK(dt >= 0, name, ": only fp32, fp16, bf16 supported");
+  TORCH_CHECK(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type() &&
+                  out.scalar_type() == q.scalar_type(),
+              name, ": q, caches and output must share one dtype");
+  TORCH_CHECK(k.sizes() == v.sizes(), name, ": k_cache and v_cache shapes differ");
+  TORCH_CHECK(out.sizes() == q.sizes(), name, ": output must match q");
+  TORCH_CHECK(k.size(0) == q.size(0) && k.size(3) == q.size(2), name, ": batch/head_dim mismatch");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && out.is_contiguous(),
+              name, ": tensors must be contiguous");
+  const int64_t B = q.size(0), Hq = q.size(1), D = q.size(2), T = k.size(1), Hkv = k.size(2);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const size_t ws_bytes = frn_gqa_decode_workspace_size(B, Hq, Hkv, D, T);
+  at::Tensor ws;
+  if (ws_bytes > 0) ws = at::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
+  check_rc(frn_gqa_decode_attention(dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                    B, Hq, Hkv, D, T, static_cast<float>(scale),
+                                    ws_bytes ? ws.data_ptr() : nullptr, ws_bytes, stream_of(q)),
+           name);
+}
+
+void gqa_decode_v2(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor out,
+                   double scale) {
+  gqa_decode_impl(q, k, v, out, scale, "gqa_decode_v2");
+}
+
+void gqa_decode_v3(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor out,
+                   int64_t group_size, double scale) {
+  TORCH_CHECK(k.dim() == 4 && group_size * k.size(2) == q.size(1),
+              "gqa_decode_v3: group_size * num_kv_heads must equal num_q_heads");
+  gqa_decode_impl(q, k, v, out, scale, "gqa_decode_v3");
+}
+
 void rmsnorm_swiglu_impl(const at::Tensor& x, const at::Tensor& raw_output, at::Tensor& output,
                          const at::Tensor& b_new, int64_t h, int64_t intermediate, double eps,
                          int threads, const char* name) {
@@ -338,6 +378,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "fused_rmsnorm_linear whose output columns are written into separate [M, n_i] tensors",
         py::arg("x"), py::arg("W_fused"), py::arg("b_new"), py::arg("eps"),
         py::arg("split_sizes"));
+  m.def("gqa_decode_v2", &gqa_decode_v2,
+        "Decode-step GQA attention into output (context split across SMs)", py::arg("q"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("output"), py::arg("scale"));
+  m.def("gqa_decode_v3", &gqa_decode_v3,
+        "Decode-step GQA attention into output (context split across SMs)", py::arg("q"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("output"), py::arg("group_size"),
+        py::arg("scale"));
   m.def("rmsnorm_swiglu", &rmsnorm_swiglu,
         "RMSNorm + SwiGLU of a [gate | up] GEMM output into output (256 threads per row)",
         py::arg("x"), py::arg("raw_output"), py::arg("output"), py::arg("b_new"), py::arg("h"),

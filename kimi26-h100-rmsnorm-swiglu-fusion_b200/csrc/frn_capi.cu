@@ -215,6 +215,55 @@ int frn_fused_rmsnorm_swiglu(int dtype, const void* x, int64_t M, int64_t K,
   return run_fused_swiglu_pair(p, intermediate, choose_swiglu_bn(M, intermediate, K, sms / 2), s);
 }
 
+static int validate_gqa(int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t T) {
+  if (dtype != FRN_DTYPE_F32 && dtype != FRN_DTYPE_F16 && dtype != FRN_DTYPE_BF16)
+    return set_error(FRN_ERR_UNSUPPORTED, "GQA decode supports fp32, fp16 and bf16");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || T <= 0)
+    return set_error(FRN_ERR_INVALID_ARGUMENT,
+                     "bad shape batch=%lld q_heads=%lld kv_heads=%lld context=%lld",
+                     (long long)B, (long long)Hq, (long long)Hkv, (long long)T);
+  if (D != 64 && D != 128)
+    return set_error(FRN_ERR_UNSUPPORTED, "head_dim must be 64 or 128 (got %lld)", (long long)D);
+  if (Hq % Hkv || Hq / Hkv > 8)
+    return set_error(FRN_ERR_UNSUPPORTED,
+                     "num_q_heads must be a multiple of num_kv_heads with a group of at most 8");
+  if (B > 65535 || Hkv > 0x7fffffffLL || T > 0x7fffffffLL || B * T * Hkv * D > (int64_t(1) << 40))
+    return set_error(FRN_ERR_UNSUPPORTED, "GQA decode dimensions too large");
+  return 0;
+}
+
+size_t frn_gqa_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                     int64_t head_dim, int64_t context_len) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int S = gqa_choose_splits(batch, num_q_heads, num_kv_heads, head_dim, context_len,
+                                  sm_count(dev), static_cast<size_t>(-1));
+  return gqa_workspace_bytes(batch, num_q_heads, head_dim, S);
+}
+
+int frn_gqa_decode_attention(int dtype, const void* q, const void* k_cache, const void* v_cache,
+                             void* out, int64_t batch, int64_t num_q_heads,
+                             int64_t num_kv_heads, int64_t head_dim, int64_t context_len,
+                             float scale, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  int rc = validate_gqa(dtype, batch, num_q_heads, num_kv_heads, head_dim, context_len);
+  if (rc) return rc;
+  if (batch == 0) return FRN_OK;
+  if (!q || !k_cache || !v_cache || !out)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "q, k_cache, v_cache and out must be non-null");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) ||
+      (workspace && !aligned16(workspace)))
+    return set_error(FRN_ERR_MISALIGNED, "q, caches, out and workspace must be 16-byte aligned");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  const size_t ws_bytes = workspace ? workspace_bytes : 0;
+  const int S = gqa_choose_splits(batch, num_q_heads, num_kv_heads, head_dim, context_len,
+                                  sm_count(dev), ws_bytes);
+  GqaProblem g{dtype, q, k_cache, v_cache, out, batch, num_q_heads, num_kv_heads, head_dim,
+               context_len, scale, workspace, ws_bytes};
+  return run_gqa_decode(g, S, static_cast<cudaStream_t>(stream));
+}
+
 size_t frn_fused_rmsnorm_linear_workspace_size(int dtype, int64_t M, int64_t N, int64_t K) {
   (void)dtype; (void)M; (void)N; (void)K;
   return 0;

@@ -97,6 +97,23 @@ int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s);
 int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws, void* q,
                       int64_t qs, float* scale, cudaStream_t s);
 
+// Decode-step grouped-query attention (frn_gqa_decode.cu).
+struct GqaProblem {
+  int dtype;
+  const void* q;  // [B, Hq, D]
+  const void* k;  // [B, T, Hkv, D]
+  const void* v;  // [B, T, Hkv, D]
+  void* out;      // [B, Hq, D]
+  int64_t B, Hq, Hkv, D, T;
+  float scale;
+  void* workspace;
+  size_t workspace_bytes;
+};
+size_t gqa_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t S);
+int gqa_choose_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t T, int sms,
+                      size_t workspace_bytes);
+int run_gqa_decode(const GqaProblem& g, int splits, cudaStream_t s);
+
 int run_rmsnorm_swiglu(int dtype, const void* x, int64_t xs, const void* raw, int64_t rs,
                        void* out, int64_t os, const void* b, int64_t rows, int64_t h,
                        int64_t inter, float eps, int threads, cudaStream_t s);

@@ -37,6 +37,7 @@ CU_SOURCES = [
     "frn_decode.cu",
     "frn_fused_linear_w8.cu",
     "frn_normalize.cu",
+    "frn_gqa_decode.cu",
 ]
 HEADERS = ["frn_ptx.cuh", "frn_internal.h"]
 

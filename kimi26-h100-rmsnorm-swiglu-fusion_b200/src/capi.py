@@ -86,6 +86,12 @@ PROTOTYPES = {
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
          c_float, c_void_p, c_int64, c_void_p],
     ),
+    "frn_gqa_decode_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64]),
+    "frn_gqa_decode_attention": (
+        c_int,
+        [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+         c_int64, c_float, c_void_p, c_size_t, c_void_p],
+    ),
     "frn_device_error": (c_int, [c_int, ctypes.POINTER(c_uint32), c_int]),
 }
 
@@ -257,6 +263,25 @@ def fused_rmsnorm_swiglu(x, w_combined, bias=None, eps: float = 1e-6, out=None):
         w_combined.stride(0), bias.data_ptr() if bias is not None else None, float(eps),
         out.data_ptr(), out.stride(0), _stream_ptr(x.device))
     check(rc, "frn_fused_rmsnorm_swiglu")
+    return out
+
+
+def gqa_decode_attention(q, k_cache, v_cache, scale: float, out=None, use_workspace=True):
+    """Decode-step GQA attention through the C ABI: q [B, Hq, D], caches
+    [B, T, Hkv, D] (contiguous); returns out [B, Hq, D]."""
+    import torch
+
+    B, Hq, D = q.shape
+    T, Hkv = k_cache.shape[1], k_cache.shape[2]
+    if out is None:
+        out = torch.empty_like(q)
+    ws_bytes = int(lib().frn_gqa_decode_workspace_size(B, Hq, Hkv, D, T)) if use_workspace else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    rc = lib().frn_gqa_decode_attention(
+        _dtype_code(q), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+        B, Hq, Hkv, D, T, float(scale), ws.data_ptr() if ws is not None else None, ws_bytes,
+        _stream_ptr(q.device))
+    check(rc, "frn_gqa_decode_attention")
     return out
 
 
