@@ -226,6 +226,28 @@ int frn_gqa_decode_attention(int dtype, const void* q, const void* k_cache, cons
                              void* stream);
 
 /*
+ * frn_gqa_decode_attention without a workspace argument and without any
+ * allocation: for callers that cannot allocate device memory at call time --
+ * hosts whose device memory is wholly reserved up front by their own
+ * allocator or memory pool, or that forbid cudaMalloc/cudaFree on their
+ * decode path -- and so cannot hand the kernel the workspace its context
+ * split needs.  The split partials go to a fixed 2 MiB scratch array inside
+ * this library (one per device, set up on first use).  A shape that needs
+ * more scratch than that (frn_gqa_decode_workspace_size > 2 MiB) is rejected
+ * with FRN_ERR_UNSUPPORTED.  Every call shares that one array, so calls whose
+ * work overlaps on the GPU (different streams, or no ordering between them)
+ * race and corrupt each other's results; issue them in order on one stream.
+ * Nothing in the scratch has to start at zero.  Same results as
+ * frn_gqa_decode_attention given its full workspace.
+ * No counterpart in the reference.
+ */
+int frn_gqa_decode_attention_noalloc(int dtype, const void* q, const void* k_cache,
+                                     const void* v_cache, void* out, int64_t batch,
+                                     int64_t num_q_heads, int64_t num_kv_heads,
+                                     int64_t head_dim, int64_t context_len, float scale,
+                                     void* stream);
+
+/*
  * Reads (and optionally clears) the device error word of `device`, which
  * kernels set when a bounded wait expires instead of hanging.  Synchronous
  * with respect to the device's legacy default stream.

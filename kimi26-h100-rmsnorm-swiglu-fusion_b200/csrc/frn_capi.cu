@@ -264,6 +264,40 @@ int frn_gqa_decode_attention(int dtype, const void* q, const void* k_cache, cons
   return run_gqa_decode(g, S, static_cast<cudaStream_t>(stream));
 }
 
+int frn_gqa_decode_attention_noalloc(int dtype, const void* q, const void* k_cache,
+                                     const void* v_cache, void* out, int64_t batch,
+                                     int64_t num_q_heads, int64_t num_kv_heads,
+                                     int64_t head_dim, int64_t context_len, float scale,
+                                     void* stream) {
+  int rc = validate_gqa(dtype, batch, num_q_heads, num_kv_heads, head_dim, context_len);
+  if (rc) return rc;
+  if (batch == 0) return FRN_OK;
+  if (!q || !k_cache || !v_cache || !out)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "q, k_cache, v_cache and out must be non-null");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+    return set_error(FRN_ERR_MISALIGNED, "q, caches and out must be 16-byte aligned");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  // Same split count (hence the same scratch need and the same result) as
+  // frn_gqa_decode_attention given its full workspace.
+  const int S = gqa_choose_splits(batch, num_q_heads, num_kv_heads, head_dim, context_len,
+                                  sm_count(dev), static_cast<size_t>(-1));
+  const size_t need = gqa_workspace_bytes(batch, num_q_heads, head_dim, S);
+  if (need > gqa_noalloc_scratch_bytes())
+    return set_error(FRN_ERR_UNSUPPORTED,
+                     "GQA decode needs %zu bytes of scratch for this shape; the static scratch "
+                     "holds %zu (use frn_gqa_decode_attention with a workspace)",
+                     need, gqa_noalloc_scratch_bytes());
+  void* scratch = nullptr;
+  if (need > 0) {
+    rc = gqa_noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+  }
+  GqaProblem g{dtype, q, k_cache, v_cache, out, batch, num_q_heads, num_kv_heads, head_dim,
+               context_len, scale, scratch, need};
+  return run_gqa_decode(g, S, static_cast<cudaStream_t>(stream));
+}
+
 size_t frn_fused_rmsnorm_linear_workspace_size(int dtype, int64_t M, int64_t N, int64_t K) {
   (void)dtype; (void)M; (void)N; (void)K;
   return 0;

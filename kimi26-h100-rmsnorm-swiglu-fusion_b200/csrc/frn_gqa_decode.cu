@@ -28,10 +28,18 @@
 
 #include <cfloat>
 #include <cstdint>
+#include <mutex>
 
 #include "frn_internal.h"
 
 namespace frn {
+
+// Scratch for frn_gqa_decode_attention_noalloc: the split partials of one
+// call live here instead of in a caller-allocated workspace.  Shared by every
+// call in the process on a given device; nothing in it needs to start at zero
+// (each call writes every slot it reads).
+constexpr size_t kGqaNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB
+static __device__ __align__(256) unsigned char g_gqa_noalloc_scratch[kGqaNoAllocScratchBytes];
 
 struct GqaParams {
   const void* q;
@@ -276,6 +284,26 @@ static int launch_gqa_d(const GqaProblem& g, int S, cudaStream_t s) {
   if (g.D == 128) return launch_gqa_t<T, 128>(g, S, s);
   return launch_gqa_t<T, 64>(g, S, s);
 }
+
+// Device address of g_gqa_noalloc_scratch, looked up once per device with
+// that device current (the caller's current device).
+int gqa_noalloc_scratch(int dev, void** ptr) {
+  static std::mutex mu;
+  static void* cache[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(FRN_ERR_UNSUPPORTED, "device %d out of range for the static scratch", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_gqa_noalloc_scratch);
+    if (e != cudaSuccess) return set_cuda_error("cudaGetSymbolAddress(GQA decode scratch)", e);
+    cache[dev] = p;
+  }
+  *ptr = cache[dev];
+  return 0;
+}
+
+size_t gqa_noalloc_scratch_bytes() { return kGqaNoAllocScratchBytes; }
 
 int run_gqa_decode(const GqaProblem& g, int splits, cudaStream_t s) {
   switch (g.dtype) {

@@ -113,6 +113,9 @@ size_t gqa_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t S);
 int gqa_choose_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t T, int sms,
                       size_t workspace_bytes);
 int run_gqa_decode(const GqaProblem& g, int splits, cudaStream_t s);
+// Static device scratch of the allocation-free GQA entry point.
+int gqa_noalloc_scratch(int dev, void** ptr);
+size_t gqa_noalloc_scratch_bytes();
 
 int run_rmsnorm_swiglu(int dtype, const void* x, int64_t xs, const void* raw, int64_t rs,
                        void* out, int64_t os, const void* b, int64_t rows, int64_t h,

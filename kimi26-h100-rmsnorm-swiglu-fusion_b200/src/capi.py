@@ -92,6 +92,11 @@ PROTOTYPES = {
         [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
          c_int64, c_float, c_void_p, c_size_t, c_void_p],
     ),
+    "frn_gqa_decode_attention_noalloc": (
+        c_int,
+        [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+         c_int64, c_float, c_void_p],
+    ),
     "frn_device_error": (c_int, [c_int, ctypes.POINTER(c_uint32), c_int]),
 }
 
@@ -282,6 +287,18 @@ def gqa_decode_attention(q, k_cache, v_cache, scale: float, out=None, use_worksp
         B, Hq, Hkv, D, T, float(scale), ws.data_ptr() if ws is not None else None, ws_bytes,
         _stream_ptr(q.device))
     check(rc, "frn_gqa_decode_attention")
+    return out
+
+
+def gqa_decode_attention_noalloc(q, k_cache, v_cache, scale: float, out):
+    """frn_gqa_decode_attention_noalloc: the library's static scratch instead of
+    a workspace; `out` must be preallocated (nothing is allocated here)."""
+    B, Hq, D = q.shape
+    T, Hkv = k_cache.shape[1], k_cache.shape[2]
+    rc = lib().frn_gqa_decode_attention_noalloc(
+        _dtype_code(q), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+        B, Hq, Hkv, D, T, float(scale), _stream_ptr(q.device))
+    check(rc, "frn_gqa_decode_attention_noalloc")
     return out
 
 
