@@ -64,3 +64,27 @@ def test_combined_and_swiglu_buffers():
     assert set(c.state_dict()) == {"W_combined", "b_combined"}
     s = fused_forward.FusedRMSNormSwiGLUV1(W, b, 12, 8, 1e-5)
     assert set(s.state_dict()) == {"W_combined", "b_combined"} and s.intermediate == 12
+
+
+def test_patch_llama_structure_on_cpu():
+    """patch_llama attaches the reference's module names and replaces the
+    forwards; building the fused modules needs no GPU."""
+    import pytest as _pytest
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from src.patch_llama import patch_llama_model
+
+    cfg = LlamaConfig(vocab_size=64, hidden_size=128, intermediate_size=256,
+                      num_hidden_layers=2, num_attention_heads=2, num_key_value_heads=1)
+    for kw, attrs in (({}, ("fused_q_proj", "fused_gate_proj")),
+                      ({"combined": True}, ("fused_qkv", "fused_gate_up")),
+                      ({"swiglu": True, "gqa_decode": True},
+                       ("fused_qkv", "fused_gate_up_swiglu", "gqa_decode_module"))):
+        model = patch_llama_model(LlamaForCausalLM(cfg), device="cpu", **kw)
+        for layer in model.model.layers:
+            owners = (layer.self_attn, layer.mlp)
+            for a in attrs:
+                assert any(hasattr(o, a) for o in owners), (kw, a)
+            assert "forward" in vars(layer) and "forward" in vars(layer.self_attn)
+    with _pytest.raises(ValueError, match="Unknown variant"):
+        patch_llama_model(LlamaForCausalLM(cfg), device="cpu", variant="V2")
