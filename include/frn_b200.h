@@ -61,6 +61,11 @@ extern "C" {
 #define FRN_KERNEL_WIDE_N192   12  /* SM pair, two accumulators: 256x(2*192)  */
 #define FRN_KERNEL_WIDE_N224   13  /* SM pair, two accumulators: 256x(2*224)  */
 #define FRN_KERNEL_WIDE_N256   14  /* SM pair, two accumulators: 256x(2*256)  */
+#define FRN_KERNEL_XRES_N128   15  /* SM pair, x resident in smem (K <= 512)   */
+#define FRN_KERNEL_XRES_N192   16  /* SM pair, x resident, 256x192 tiles       */
+#define FRN_KERNEL_XRES_N224   17  /* SM pair, x resident, 256x224 tiles       */
+#define FRN_KERNEL_XRES_N256   18  /* SM pair, x resident, 256x256 tiles       */
+#define FRN_KERNEL_XRES_AUTO   19  /* SM pair, x resident, width by (M, N, K)  */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */

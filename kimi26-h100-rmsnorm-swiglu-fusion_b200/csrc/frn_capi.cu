@@ -330,6 +330,15 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
     static const int bns[4] = {128, 192, 224, 256};
     return run_fused_linear_pair(p, PairChoice{bns[kernel - FRN_KERNEL_WIDE_N128], 2}, s);
   }
+  if (kernel >= FRN_KERNEL_XRES_N128 && kernel <= FRN_KERNEL_XRES_AUTO) {
+    if (K > 512)
+      return set_error(FRN_ERR_UNSUPPORTED, "the x-resident kernel takes K <= 512 (got %lld)",
+                       (long long)K);
+    static const int bns[4] = {128, 192, 224, 256};
+    const int bn = kernel == FRN_KERNEL_XRES_AUTO ? choose_xres_bn(M, N, K, sms / 2)
+                                                  : bns[kernel - FRN_KERNEL_XRES_N128];
+    return run_fused_linear_xres(p, bn, s);
+  }
   if (kernel == FRN_KERNEL_DECODE) {
     if (M > 128)
       return set_error(FRN_ERR_UNSUPPORTED, "the decode kernel takes M <= 128 (got %lld)",

@@ -164,10 +164,23 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     // Four issuing threads (a single thread keeps only a few bulk-tensor
     // loads in flight): W / x, each over even / odd stages.
     if (lane == 0) {
-      griddep_wait();
       const uint32_t pid = warp - C::WARP_PROD0;
       const bool is_w = (pid & 1u) == 0;
       const uint32_t parity_sel = pid >> 1;
+      // Warm L2 with this thread's first ring of tiles while the preceding
+      // grid drains (see tma_prefetch_2d).
+      for (int i = static_cast<int>(parity_sel); i < nkb && i < STAGES; i += 2) {
+        const int kc = (kb_begin + i) * C::BK;
+        if (!is_w) {
+          tma_prefetch_2d(&tmap_x, kc, 0);
+        } else if (SWIGLU) {
+          tma_prefetch_2d(&tmap_w, kc, n0);
+          tma_prefetch_2d(&tmap_w, kc, p.up_row0 + n0);
+        } else {
+          tma_prefetch_2d(&tmap_w, kc, n0);
+        }
+      }
+      griddep_wait();
       uint32_t stage = 0, phase = 0;
       for (int i = 0; i < nkb; ++i) {
         if ((stage & 1u) != parity_sel) {

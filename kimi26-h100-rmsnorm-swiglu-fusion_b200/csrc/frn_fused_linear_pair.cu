@@ -32,32 +32,10 @@
 #include <cstdint>
 
 #include "frn_internal.h"
+#include "frn_pair_common.cuh"
 #include "frn_ptx.cuh"
 
 namespace frn {
-
-// Output tensor maps: [32 rows x 64 columns] store boxes (128B swizzle), one
-// per output part, plus a [32 x 32] box (64B swizzle) for tiles whose last
-// chunk is 32 columns wide (single output only).
-struct PairOut {
-  CUtensorMap map[kMaxParts];
-  CUtensorMap half;
-  int32_t col0[kMaxParts];  // first output column of each part
-  int32_t nparts;
-};
-
-struct PairParams {
-  int32_t M, N, K;
-  int32_t num_m_blocks;  // of 256 rows
-  int32_t num_n_blocks;  // of BN columns
-  int32_t num_k_blocks;  // of 64
-  float eps;
-  const void* bias;  // may be null
-  void* out;
-  int64_t out_row_stride;  // elements
-  int32_t up_row0;         // SwiGLU: first W row of the up block (= intermediate)
-  uint64_t timeout_ns;
-};
 
 // NACC accumulators of BN columns per pair tile: NACC = 1 double-buffers the
 // accumulator in TMEM (tile i's epilogue overlaps tile i+1's mainloop); NACC
@@ -188,10 +166,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
     // Four issuing threads: a single thread keeps only a few bulk-tensor loads
     // in flight, so x and W loads are split by operand and by stage parity.
     if (lane == 0) {
-      griddep_wait();
       const uint32_t pid = warp - C::WARP_PROD0;
       const bool is_a = (pid & 1u) == 0;
       const uint32_t parity_sel = pid >> 1;  // this thread fills stages with s % 2 == parity_sel
+      if (t_begin < t_end) {
+        // While the preceding grid drains, pull this thread's first ring of
+        // tiles into L2 so the first loads after the wait do not go to HBM.
+        const int pm0 = (t_begin / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
+        const int pn0 = (t_begin % p.num_n_blocks) * OUT_N + rank * C::BN_HALF;
+        for (int kb = static_cast<int>(parity_sel); kb < nkb && kb < STAGES; kb += 2) {
+          if (is_a) {
+            tma_prefetch_2d(&tmap_x, kb * C::BK, pm0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < NACC; ++j)
+              tma_prefetch_2d(&tmap_w, kb * C::BK,
+                              SWIGLU ? (j == 0 ? pn0 : p.up_row0 + pn0) : pn0 + j * BN);
+          }
+        }
+      }
+      griddep_wait();
       const bool arms = is_a && rank == 0;
       uint32_t stage = 0, phase = 0;
       for (int t = t_begin; t < t_end; ++t) {
@@ -376,58 +370,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         }
         continue;
       }
-      const uint32_t taddr = tmem_base + acc * C::TILE_N + ((q * 32u) << 16);
-#pragma unroll 1
-      for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
-        // 64 columns (the last chunk may be 32): TMEM -> fp32 -> scale/bias ->
-        // one rounding -> swizzled smem block -> TMA store, which clips rows
-        // >= M and columns >= N.
-        const bool half = C::HALF_TAIL && c == C::NCHUNK - 1;
-        const int col0 = n0 + c * 64;
-        uint4 bv[8];
-        if (has_bias) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            bv[j] = (col0 + j * 8 < p.N && !(half && j >= 4))
-                        ? ld_global_nc_v4(bias + col0 + j * 8)
-                        : make_uint4(0u, 0u, 0u, 0u);
-        }
-        uint32_t v[64];
-        tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_ld_wait();
-        if (c == C::NCHUNK - 1 && reuse_acc) {
-          // Only a later tile of this pair waits for this accumulator; the
-          // last NBUF tiles send nothing, so no remote arrive is in flight
-          // when the pair leaves.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
-        }
-        uint8_t* sbp = smem + C::OFF_STG + (q * 2 + (nst & 1u)) * C::STG_BYTES;
-        const uint32_t sb = smem_addr(sbp);
-        // The TMA store issued two chunks ago read this buffer; at most the
-        // previous chunk's store may still be reading smem.
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        if (half) {
-          if (has_bias) stage_rows_swizzled<T, 4, true>(v, inv_rms, bv, sb, lane);
-          else stage_rows_swizzled<T, 4, false>(v, inv_rms, bv, sb, lane);
-        } else {
-          if (has_bias) stage_rows_swizzled<T, 8, true>(v, inv_rms, bv, sb, lane);
-          else stage_rows_swizzled<T, 8, false>(v, inv_rms, bv, sb, lane);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          // Part of this chunk (a chunk never straddles two parts: split
-          // outputs take 64-column multiples for parts and tiles).
-          int pi = 0;
-          while (pi + 1 < outm.nparts && col0 >= outm.col0[pi + 1]) ++pi;
-          tma_store_2d(half ? &outm.half : &outm.map[pi], sbp, col0 - outm.col0[pi], row_base);
-          bulk_commit_group();
-        }
-      }
+      pair_store_linear_tile<T, C::TILE_N>(smem + C::OFF_STG, q, lane,
+                                            tmem_base + acc * C::TILE_N + ((q * 32u) << 16),
+                                            n0, row_base, inv_rms, has_bias ? bias : nullptr, p.N,
+                                            outm, nst, reuse_acc, leader_tmem_empty0 + acc * 8);
     }
     // The staging blocks must not be released while a store still reads them;
     // the global writes themselves are complete when the grid is.
@@ -500,35 +446,10 @@ static int launch_pair(const LinearProblem& pr, cudaStream_t stream, int64_t int
   // Output: one warp's [32 rows x 64 columns] block per store (128B swizzle),
   // and [32 x 32] with the 64B swizzle for a tile whose last chunk is 32 wide.
   PairOut outm;
-  if (pr.parts && pr.parts->n > 1) {
-    if (SWIGLU || OUT_N % 64 != 0)
-      return set_error(FRN_ERR_UNSUPPORTED, "split output needs a tile width multiple of 64");
-    outm.nparts = pr.parts->n;
-    for (int i = 0; i < pr.parts->n; ++i) {
-      rc = encode_tmap_2d(&outm.map[i], dt, 2, pr.parts->out[i], pr.parts->cols[i], pr.M,
-                          pr.parts->stride[i], 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
-      if (rc) return rc;
-      outm.col0[i] = static_cast<int32_t>(pr.parts->col0[i]);
-    }
-    outm.half = outm.map[0];
-  } else {
-    outm.nparts = 1;
-    outm.col0[0] = 0;
-    rc = encode_tmap_2d(&outm.map[0], dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 64, 32,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-    if (OUT_N % 64 != 0) {
-      rc = encode_tmap_2d(&outm.half, dt, 2, pr.out, n_out, pr.M, pr.out_row_stride, 32, 32,
-                          CU_TENSOR_MAP_SWIZZLE_64B);
-      if (rc) return rc;
-    } else {
-      outm.half = outm.map[0];
-    }
-  }
-  for (int i = outm.nparts; i < kMaxParts; ++i) {
-    outm.map[i] = outm.map[0];
-    outm.col0[i] = 0x7fffffff;
-  }
+  if (SWIGLU && pr.parts && pr.parts->n > 1)
+    return set_error(FRN_ERR_UNSUPPORTED, "split output is for the linear op only");
+  rc = build_pair_out(pr, n_out, OUT_N % 64 != 0, &outm);
+  if (rc) return rc;
 
   PairParams p;
   p.M = static_cast<int32_t>(pr.M);

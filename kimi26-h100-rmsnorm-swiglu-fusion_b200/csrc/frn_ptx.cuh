@@ -102,6 +102,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Warms L2 with a 2-D tile (no shared memory written, nothing to wait for).
+// Safe before griddepcontrol.wait: L2 is the coherence point, so a line
+// fetched before the preceding grid writes it is simply updated by that write.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 // 2-D tiled TMA store from shared memory (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* smem_src,
                                              int32_t c0, int32_t c1) {

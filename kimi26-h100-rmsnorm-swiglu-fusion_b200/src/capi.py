@@ -40,6 +40,11 @@ FRN_KERNEL_WIDE_N128 = 11
 FRN_KERNEL_WIDE_N192 = 12
 FRN_KERNEL_WIDE_N224 = 13
 FRN_KERNEL_WIDE_N256 = 14
+FRN_KERNEL_XRES_N128 = 15
+FRN_KERNEL_XRES_N192 = 16
+FRN_KERNEL_XRES_N224 = 17
+FRN_KERNEL_XRES_N256 = 18
+FRN_KERNEL_XRES_AUTO = 19
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {
