@@ -259,6 +259,17 @@ int frn_gqa_decode_attention_noalloc(int dtype, const void* q, const void* k_cac
  */
 int frn_device_error(int device, uint32_t* flags, int clear);
 
+/*
+ * Failure-detection self-test: launches a one-thread kernel on `stream` that
+ * waits on an mbarrier nothing ever arrives at, using the bounded wait of
+ * every pipeline role in this library.  After timeout_ms (1..10000) the wait
+ * gives up, sets FRN_DEVERR_WAIT_TIMEOUT in the device error word and the
+ * kernel returns normally (no trap; the context stays usable).  Read the word
+ * with frn_device_error.  No counterpart in the reference, whose launchers
+ * have no device-side failure reporting.
+ */
+int frn_selftest_wait_timeout(int timeout_ms, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -20,6 +20,20 @@ __device__ uint32_t g_frn_device_error = 0u;
 
 static thread_local char t_last_error[512] = {0};
 
+// Failure-detection self-test: one thread waits, with the same bounded
+// mbarrier wait every pipeline role uses, on a barrier nothing arrives at.
+// The wait gives up after timeout_ns, ORs kDevErrWaitTimeout into the device
+// error word and the kernel returns; no trap, the context stays usable.
+__global__ void selftest_wait_timeout_kernel(uint64_t timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t abort_flag;
+  if (threadIdx.x != 0) return;
+  abort_flag = 0u;
+  mbar_init(&bar, 1);
+  fence_mbarrier_init();
+  mbar_wait(&bar, 0, &abort_flag, timeout_ns);
+}
+
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -453,6 +467,16 @@ int frn_quantize_int8_per_channel(int dtype, const void* w, int64_t N, int64_t K
     return set_error(FRN_ERR_UNSUPPORTED, "dimension exceeds 2^31-1");
   return run_quantize_int8(dtype, w, N, K, w_row_stride, q, q_row_stride, scale,
                            static_cast<cudaStream_t>(stream));
+}
+
+int frn_selftest_wait_timeout(int timeout_ms, void* stream) {
+  if (timeout_ms <= 0 || timeout_ms > 10000)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "timeout_ms must be in 1..10000");
+  selftest_wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint64_t>(timeout_ms) * 1000000ull);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("launch selftest_wait_timeout", e);
+  return FRN_OK;
 }
 
 int frn_device_error(int device, uint32_t* flags, int clear) {

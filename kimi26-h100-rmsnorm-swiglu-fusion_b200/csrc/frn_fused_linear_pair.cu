@@ -370,7 +370,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<BN, STAGES, 
         }
         continue;
       }
-      pair_store_linear_tile<T, C::TILE_N>(smem + C::OFF_STG, q, lane,
+      pair_store_linear_tile<T, C::TILE_N>(smem + C::OFF_STG + q * 2 * C::STG_BYTES, lane,
                                             tmem_base + acc * C::TILE_N + ((q * 32u) << 16),
                                             n0, row_base, inv_rms, has_bias ? bias : nullptr, p.N,
                                             outm, nst, reuse_acc, leader_tmem_empty0 + acc * 8);

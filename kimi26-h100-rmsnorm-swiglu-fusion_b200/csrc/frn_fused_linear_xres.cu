@@ -291,7 +291,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(XresCfg<BN, BSTAGES>
         __syncwarp();
         if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
       }
-      pair_store_linear_tile<T, BN>(smem + C::OFF_STG, q, lane,
+      pair_store_linear_tile<T, BN>(smem + C::OFF_STG + q * 2 * C::STG_BYTES, lane,
                                     tmem_base + acc * BN + ((q * 32u) << 16), n0, row_base,
                                     inv_rms, bias, p.N, outm, nst, t + 2 < t_end,
                                     leader_tmem_empty0 + acc * 8);

@@ -76,27 +76,31 @@ inline int build_pair_out(const LinearProblem& pr, int64_t n_out, bool half_tail
   return 0;
 }
 
-// Epilogue of one linear pair tile for epilogue warp q (TMEM lanes
-// [32q, 32q+32) = rows row_base .. row_base+31 of this CTA's half): for each
-// 64-column chunk (the last may be 32 wide), TMEM -> fp32 -> acc * inv_rms
-// (+ b) -> one rounding -> 128B-swizzled [32 x 64] smem block (double-
-// buffered per warp at stg + (2q + nst % 2) * 4 KB) -> TMA tensor store through
-// the output part's map, which also clips rows >= M and columns >= N.  After
-// the last TMEM read the warp releases the accumulator on `tmem_empty_remote`
-// (the even CTA's barrier) if `release_acc`.
+// Epilogue of one linear pair tile for a warp whose TMEM lane quarter holds
+// rows row_base .. row_base+31 of this CTA's half (taddr points at that
+// quarter of the accumulator): for each 64-column chunk c (the last may be 32
+// wide) with c % chunk_mod == chunk_sel, TMEM -> fp32 -> acc * inv_rms (+ b)
+// -> one rounding -> 128B-swizzled [32 x 64] smem block (double-buffered at
+// stg + (nst % 2) * 4 KB) -> TMA tensor store through the output part's map,
+// which also clips rows >= M and columns >= N.  After its last TMEM read the
+// warp releases the accumulator on `tmem_empty_remote` (the even CTA's
+// barrier) if `release_acc`.
 template <typename T, int TILE_N>
-__device__ __forceinline__ void pair_store_linear_tile(uint8_t* stg, uint32_t q, uint32_t lane,
+__device__ __forceinline__ void pair_store_linear_tile(uint8_t* stg, uint32_t lane,
                                                        uint32_t taddr, int n0, int row_base,
                                                        float inv_rms, const T* bias, int N,
                                                        const PairOut& outm, uint32_t& nst,
                                                        bool release_acc,
-                                                       uint32_t tmem_empty_remote) {
+                                                       uint32_t tmem_empty_remote,
+                                                       int chunk_mod = 1, int chunk_sel = 0) {
   constexpr int NCHUNK = (TILE_N + 63) / 64;
   constexpr bool HALF_TAIL = TILE_N % 64 != 0;
   constexpr int STG_BYTES = 32 * 128;
   const bool has_bias = bias != nullptr;
+  int c_last = NCHUNK - 1;  // this warp's last chunk
+  while (c_last % chunk_mod != chunk_sel) --c_last;
 #pragma unroll 1
-  for (int c = 0; c < NCHUNK; ++c, ++nst) {
+  for (int c = chunk_sel; c < NCHUNK; c += chunk_mod, ++nst) {
     const bool half = HALF_TAIL && c == NCHUNK - 1;
     const int col0 = n0 + c * 64;
     uint4 bv[8];
@@ -110,12 +114,12 @@ __device__ __forceinline__ void pair_store_linear_tile(uint8_t* stg, uint32_t q,
     tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
     if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
     tmem_ld_wait();
-    if (c == NCHUNK - 1 && release_acc) {
+    if (c == c_last && release_acc) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster_relaxed(tmem_empty_remote);
     }
-    uint8_t* sbp = stg + (q * 2 + (nst & 1u)) * STG_BYTES;
+    uint8_t* sbp = stg + (nst & 1u) * STG_BYTES;
     const uint32_t sb = smem_addr(sbp);
     // The TMA store issued two chunks ago read this buffer; at most the
     // previous chunk's store may still be reading smem.

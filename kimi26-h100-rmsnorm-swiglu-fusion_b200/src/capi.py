@@ -103,6 +103,7 @@ PROTOTYPES = {
          c_int64, c_float, c_void_p],
     ),
     "frn_device_error": (c_int, [c_int, ctypes.POINTER(c_uint32), c_int]),
+    "frn_selftest_wait_timeout": (c_int, [c_int, c_void_p]),
 }
 
 _lib = None
@@ -305,6 +306,11 @@ def gqa_decode_attention_noalloc(q, k_cache, v_cache, scale: float, out):
         B, Hq, Hkv, D, T, float(scale), _stream_ptr(q.device))
     check(rc, "frn_gqa_decode_attention_noalloc")
     return out
+
+
+def selftest_wait_timeout(timeout_ms: int, stream=None) -> None:
+    """Launch the bounded-wait self-test kernel (see include/frn_b200.h)."""
+    check(lib().frn_selftest_wait_timeout(int(timeout_ms), stream), "frn_selftest_wait_timeout")
 
 
 def device_error(device: int = 0, clear: bool = False) -> int:

@@ -95,3 +95,68 @@ def test_gloo_world2_token_and_column_parallel():
         p.join(90)
         assert p.exitcode == 0
     assert dict(results) == {0: (True, True, True), 1: (True, True, True)}
+
+
+# ------------------------------------------------ failure detection (host side)
+
+
+def _never_joined(port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=0, world_size=2,
+                                timeout=datetime.timedelta(seconds=3))
+        q.put("joined")
+    except Exception as e:  # the peer never connects: init must give up
+        q.put(type(e).__name__)
+
+
+@pytest.mark.timeout(120)
+def test_gloo_rank_that_never_joins_times_out():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_never_joined, args=(_free_port(), q))
+    p.start()
+    p.join(90)
+    assert p.exitcode == 0
+    assert q.get(timeout=5) != "joined"
+
+
+def _gather_after_peer_left(rank, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=5))
+    x, gamma, W = orc.make_inputs(8, 32, 16, seed=1, dtype=torch.float32)
+    Wn = orc.fold_gamma(W, gamma)
+    if rank == 1:
+        os._exit(0)  # leaves between steps, with no collective in flight
+    try:
+        multigpu.fused_rmsnorm_linear_token_parallel(x, Wn, None, orc.EPS, gather=True,
+                                                     op=_cpu_op)
+        q.put("gathered")
+    except Exception as e:
+        q.put(type(e).__name__)
+    os._exit(0)
+
+
+@pytest.mark.timeout(120)
+def test_token_parallel_gather_fails_when_a_rank_left():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_after_peer_left, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+    assert all(p.exitcode == 0 for p in procs)
+    assert q.get(timeout=5) != "gathered"
