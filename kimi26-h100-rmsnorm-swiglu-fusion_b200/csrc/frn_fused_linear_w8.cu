@@ -71,7 +71,8 @@ struct W8Cfg {
   static constexpr int EPI_WARPS = 4, RMS_WARPS = 4, CONV_WARPS = 4;
   static constexpr int WARP_PROD0 = 4, WARP_MMA = 6, WARP_RMS0 = 7, WARP_CONV0 = 11;
   static constexpr int THREADS = 32 * 15;
-  static_assert(STAGES % 2 == 0, "stages are split between two producers");
+  // Producers take stages by parity and converters k-blocks by sequence, so
+  // any ring depth works; an odd one leaves one producer a stage more.
   static_assert(B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "stage buffers must stay aligned");
   static_assert(OFF_STG % 1024 == 0, "staging blocks must be 1024-aligned for the 128B swizzle");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
@@ -260,20 +261,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
       mbar_wait(drain, 0, &zero, to);
     }
   } else if (warp >= C::WARP_CONV0) {
-    // Converter warp cw widens the k-blocks held in stages s with
-    // s % CONV_WARPS == cw (so up to CONV_WARPS stages convert at once): lane l
+    // Converter warp cw widens every CONV_WARPS-th k-block of the sequence
+    // (up to CONV_WARPS stages convert at once, for any ring depth): lane l
     // takes rows l, l+32, ... of this CTA's int8 half-tile, then lane 0
-    // publishes the stage on the even CTA's `conv` barrier (one arrival per
-    // CTA).
+    // publishes the stage on the even CTA's `conv` barrier.
     const uint32_t cw = warp - C::WARP_CONV0;
     const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
     const uint32_t leader_sink = mapa_shared(smem_addr(tmem_slot + 2), 0);
     const uint32_t q0 = smem_addr(smem + C::OFF_Q), b0 = smem_addr(smem + C::OFF_B);
-    uint32_t stage = 0, phase = 0;
+    uint32_t stage = 0, phase = 0, seq = 0;
     bool ok = true;
     for (int t = t_begin; t < t_end && ok; ++t) {
-      for (int kb = 0; kb < nkb; ++kb) {
-        if (stage % C::CONV_WARPS == cw) {
+      for (int kb = 0; kb < nkb; ++kb, ++seq) {
+        if (seq % C::CONV_WARPS == cw) {
           if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
           const uint32_t qs = q0 + stage * C::Q_BYTES, bs = b0 + stage * C::B_BYTES;
 #pragma unroll 2
@@ -579,15 +579,30 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
   return 0;
 }
 
+// Tile width for the int8 kernel: the fewest tensor-core columns on the
+// busiest pair, ceil(tiles / pairs) * bn (ties to the wider tile); widths up to
+// 224 get a five-stage ring, 256 fits only four.
+static int choose_w8_bn(int64_t M, int64_t N, int pairs) {
+  static const int cands[] = {256, 224, 192, 128};
+  const int64_t mb = (M + 255) / 256;
+  int pick = 256;
+  double best = 1e300;
+  for (int bn : cands) {
+    const int64_t tiles = mb * ((N + bn - 1) / bn);
+    const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * bn *
+                        (bn == 256 ? 1.1 : 1.0);  // the shallower ring
+    if (cost < best * 0.999) { best = cost; pick = bn; }
+  }
+  return pick;
+}
+
 template <typename T>
 static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
-  const int bn = choose_pair_tiling(pr.M, pr.N, pr.K, sm_count(0) / 2).bn;
-  switch (bn) {
+  switch (choose_w8_bn(pr.M, pr.N, sm_count(0) / 2)) {
     case 256: return launch_w8<T, 256, 4>(pr, s);
-    case 224: return launch_w8<T, 224, 4>(pr, s);
-    case 192: return launch_w8<T, 192, 4>(pr, s);
-    case 160: return launch_w8<T, 160, 4>(pr, s);
-    default: return launch_w8<T, 128, 4>(pr, s);
+    case 224: return launch_w8<T, 224, 5>(pr, s);
+    case 192: return launch_w8<T, 192, 5>(pr, s);
+    default: return launch_w8<T, 128, 6>(pr, s);
   }
 }
 
