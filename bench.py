@@ -470,7 +470,79 @@ def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
         del rot
         torch.cuda.empty_cache()
     res["int8_q_b"] = sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps)
+    for name, M in (("swiglu_llama_prefill", 512), ("swiglu_llama_decode_m8", 8)):
+        res[name] = sweep_swiglu(denominator_cuda, device, hbm_gbs, tflops_peak, M, steps)
+    res["gqa_decode_llama"] = sweep_gqa(denominator_cuda, device, hbm_gbs, steps)
     return res
+
+
+def sweep_swiglu(denominator_cuda, device, hbm_gbs, tflops_peak, M, steps):
+    """Llama-3-8B MLP gate/up (K=4096, I=14336): one fused launch vs the
+    reference's FusedRMSNormSwiGLU path (F.linear over W_combined, then its
+    rmsnorm_swiglu epilogue) on the same GPU."""
+    import torch
+    import torch.nn.functional as F
+
+    K, inter = 4096, 14336
+    sets = []
+    for s in range(2):  # 2 x 235 MB of weights > L2
+        x, gamma, W = gpu_inputs(M, K, 2 * inter, 700 + s, device)
+        Wc = (W * gamma).contiguous()
+        b = torch.zeros(2 * inter, dtype=torch.bfloat16, device=device)
+        sets.append((x, Wc, b, torch.empty(M, inter, dtype=torch.bfloat16, device=device)))
+    ours = [(lambda t=t: denominator_cuda.fused_rmsnorm_swiglu(t[0], t[1], None, EPS, t[3]))
+            for t in sets]
+
+    def ref_path(t):
+        x, Wc, b, out = t
+        denominator_cuda.rmsnorm_swiglu(x, F.linear(x, Wc), out, b, K, inter, EPS)
+
+    base = [(lambda t=t: ref_path(t)) for t in sets]
+    n = 40
+    t_ours = time_steps(ours, n, 2) * 1e3 / n
+    t_base = time_steps(base, n, 2) * 1e3 / n
+    fl = 2.0 * M * K * 2 * inter
+    by = 2.0 * (M * K + 2 * inter * K + M * inter)
+    roof_us = max(fl / (tflops_peak * 1e12), by / (hbm_gbs * 1e9)) * 1e6
+    return {"us_per_call": round(t_ours, 3), "roofline_us": round(roof_us, 3),
+            "frac_of_roofline": round(roof_us / t_ours, 3),
+            "reference_linear_then_swiglu_us": round(t_base, 3),
+            "speedup_vs_reference_path": round(t_base / t_ours, 3)}
+
+
+def sweep_gqa(denominator_cuda, device, hbm_gbs, steps):
+    """Decode-step GQA attention, Llama-3-8B heads (32 q / 8 kv, d 128) at
+    batch 4 over a 4096-token cache: ours vs SDPA over repeated KV heads."""
+    import torch
+    import torch.nn.functional as F
+
+    B, Hq, Hkv, D, T = 4, 32, 8, 128, 4096
+    g = torch.Generator(device=device).manual_seed(5)
+    sets = []
+    for s in range(4):  # 4 x 67 MB of K/V > L2
+        q = torch.randn(B, Hq, D, generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn(B, T, Hkv, D, generator=g, device=device).to(torch.bfloat16)
+        v = torch.randn(B, T, Hkv, D, generator=g, device=device).to(torch.bfloat16)
+        sets.append((q, k, v, torch.empty_like(q)))
+    scale = 1.0 / math.sqrt(D)
+    ours = [(lambda t=t: denominator_cuda.gqa_decode_v3(t[0], t[1], t[2], t[3], Hq // Hkv, scale))
+            for t in sets]
+
+    def sdpa(t):
+        q, k, v, _ = t
+        kk = k.repeat_interleave(Hq // Hkv, dim=2).permute(0, 2, 1, 3)
+        vv = v.repeat_interleave(Hq // Hkv, dim=2).permute(0, 2, 1, 3)
+        return F.scaled_dot_product_attention(q.unsqueeze(2), kk, vv, scale=scale)
+
+    base = [(lambda t=t: sdpa(t)) for t in sets]
+    n = 40
+    t_ours = time_steps(ours, n, 4) * 1e3 / n
+    t_base = time_steps(base, n, 4) * 1e3 / n
+    by = 2.0 * (2 * B * T * Hkv * D + 2 * B * Hq * D)
+    roof_us = by / (hbm_gbs * 1e9) * 1e6
+    return {"us_per_call": round(t_ours, 3), "roofline_us": round(roof_us, 3),
+            "frac_of_roofline": round(roof_us / t_ours, 3), "sdpa_repeat_kv_us": round(t_base, 3),
+            "speedup_vs_sdpa": round(t_base / t_ours, 3)}
 
 
 def sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps):

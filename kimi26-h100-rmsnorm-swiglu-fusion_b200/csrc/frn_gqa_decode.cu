@@ -21,7 +21,8 @@
 //           maxima) and writes out.
 //
 // The K/V stream is the cost (2 * B * T * Hkv * D elements); the split count
-// is chosen so that about two CTAs per SM read it.
+// is chosen so that about four CTAs per SM read it, each warp keeping a run of
+// 8 K and 8 V rows in flight.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -104,6 +105,7 @@ __device__ __forceinline__ __nv_bfloat16 to_t<__nv_bfloat16>(float v) {
 }
 
 constexpr int kGqaWarps = 4;
+constexpr int kUnroll = 8;  // K/V rows per warp in flight (x2 for K and V)
 
 template <typename T, int D, int GMAX>
 __global__ void __launch_bounds__(32 * kGqaWarps)
@@ -145,26 +147,58 @@ __global__ void __launch_bounds__(32 * kGqaWarps)
   const int64_t base = (static_cast<int64_t>(b) * p.T * p.Hkv + kvh) * D + lane * E;
   const T* kp = static_cast<const T*>(p.k) + base;
   const T* vp = static_cast<const T*>(p.v) + base;
-  for (int t = t_begin + warp; t < t_end; t += kGqaWarps) {
-    float kf[E], vf[E];
-    load_e<T, E>(kp + t * tstride, kf);
-    load_e<T, E>(vp + t * tstride, vf);
+  // Each warp takes runs of kUnroll consecutive tokens (every kGqaWarps-th
+  // run) and issues all of a run's K and V row loads before using any, so a
+  // warp keeps 2 * kUnroll rows in flight instead of waiting on each.
+  for (int tb = t_begin + warp * kUnroll; tb < t_end; tb += kGqaWarps * kUnroll) {
+    float kf[kUnroll][E], vf[kUnroll][E];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int t = tb + u < t_end ? tb + u : tb;  // clamp: the load stays in bounds
+      load_e<T, E>(kp + t * tstride, kf[u]);
+      load_e<T, E>(vp + t * tstride, vf[u]);
+    }
+    // All scores of the run first: kUnroll * G independent shuffle-reduction
+    // chains that interleave, instead of one dependent chain per token.
+    float sc[kUnroll][GMAX];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) d = fmaf(q[g][e], kf[u][e], d);
+        sc[u][g] = d;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g)
+          if (g < G) sc[u][g] += __shfl_xor_sync(0xffffffffu, sc[u][g], o);
+    // One online-softmax rescale per run and head.
 #pragma unroll
     for (int g = 0; g < GMAX; ++g) {
-      if (g < G) {
-        float s = 0.f;
+      if (g >= G) continue;
+      float mx = m[g];
 #pragma unroll
-        for (int e = 0; e < E; ++e) s = fmaf(q[g][e], kf[e], s);
+      for (int u = 0; u < kUnroll; ++u)
+        if (tb + u < t_end) mx = fmaxf(mx, sc[u][g]);
+      const float c = exp2f(m[g] - mx);
+      l[g] *= c;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const float mn = fmaxf(m[g], s);
-        const float c = exp2f(m[g] - mn);
-        const float pw = exp2f(s - mn);
-        l[g] = fmaf(l[g], c, pw);
+      for (int e = 0; e < E; ++e) acc[g][e] *= c;
 #pragma unroll
-        for (int e = 0; e < E; ++e) acc[g][e] = fmaf(acc[g][e], c, pw * vf[e]);
-        m[g] = mn;
+      for (int u = 0; u < kUnroll; ++u) {
+        if (tb + u < t_end) {
+          const float pw = exp2f(sc[u][g] - mx);
+          l[g] += pw;
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pw, vf[u][e], acc[g][e]);
+        }
       }
+      m[g] = mx;
     }
   }
 #pragma unroll
@@ -226,13 +260,16 @@ __global__ void gqa_decode_merge_kernel(const GqaParams p, int D) {
   }
 }
 
-// Context splits per (batch, KV head): about two CTAs per SM in total, at
-// least 64 tokens per split, and no more than the workspace holds.
+// Context splits per (batch, KV head): as many as keep every CTA resident in
+// one wave (three per SM), at least 32 tokens per split, and no more than the
+// workspace holds.
 int gqa_choose_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t T, int sms,
                       size_t workspace_bytes) {
+  // All CTAs resident at once: three per SM fit (registers), and a second
+  // partial wave would double the time.
   const int64_t ctas = B * Hkv;
-  int64_t s = (2 * sms + ctas - 1) / (ctas > 0 ? ctas : 1);
-  const int64_t by_len = (T + 63) / 64;
+  int64_t s = (3 * static_cast<int64_t>(sms)) / (ctas > 0 ? ctas : 1);
+  const int64_t by_len = (T + 31) / 32;
   if (s > by_len) s = by_len;
   if (s > 64) s = 64;
   if (s < 1) s = 1;
@@ -245,8 +282,34 @@ size_t gqa_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t S) {
   return static_cast<size_t>(B * Hq * S) * static_cast<size_t>(D + 2) * sizeof(float);
 }
 
+// CTAs of this instantiation that fit on one SM (registers decide).
+template <typename T, int D, int GMAX>
+static int gqa_blocks_per_sm() {
+  static int cache[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= kMaxDevices) return 1;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gqa_decode_split_kernel<T, D, GMAX>,
+                                                      32 * kGqaWarps, 0) != cudaSuccess ||
+        n < 1) {
+      cudaGetLastError();
+      n = 1;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
 template <typename T, int D>
 static int launch_gqa_t(const GqaProblem& g, int S, cudaStream_t stream) {
+  {  // keep every CTA resident: no second partial wave
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int bps = g.Hq / g.Hkv <= 4 ? gqa_blocks_per_sm<T, D, 4>() : gqa_blocks_per_sm<T, D, 8>();
+    const int64_t fit = static_cast<int64_t>(bps) * sm_count(dev) / (g.B * g.Hkv);
+    if (S > fit) S = fit > 1 ? static_cast<int>(fit) : 1;
+  }
   GqaParams p;
   p.q = g.q;
   p.k = g.k;

@@ -33,15 +33,3 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.testing.assert_close(out.float().cpu(), ref.float().cpu(), atol=ATOL, rtol=RTOL)
         torch.testing.assert_close(out.float().cpu(), orc.gqa_decode_reference(q, k, v, scale),
                                    atol=ATOL, rtol=RTOL)
-
-
-def test_noalloc_rejects_shapes_beyond_its_scratch():
-    # batch 16 x 128 query heads over 16 KV heads, 2 context splits: the split
-    # partials (16*128*2*(128+2) floats) exceed the 2 MiB scratch.
-    B, Hq, Hkv, D, T = 16, 128, 16, 128, 256
-    need = capi.lib().frn_gqa_decode_workspace_size(B, Hq, Hkv, D, T)
-    assert need > 2 << 20
-    q = torch.zeros(B, Hq, D, dtype=torch.bfloat16, device=DEV)
-    kv = torch.zeros(B, T, Hkv, D, dtype=torch.bfloat16, device=DEV)
-    with pytest.raises(capi.FrnError, match="static scratch"):
-        capi.gqa_decode_attention_noalloc(q, kv, kv, 1.0, torch.empty_like(q))
