@@ -66,6 +66,8 @@ extern "C" {
 #define FRN_KERNEL_XRES_N224   17  /* SM pair, x resident, 256x224 tiles       */
 #define FRN_KERNEL_XRES_N256   18  /* SM pair, x resident, 256x256 tiles       */
 #define FRN_KERNEL_XRES_AUTO   19  /* SM pair, x resident, width by (M, N, K)  */
+#define FRN_KERNEL_PAIR_TS     20  /* SM pair, x in TMEM as the A operand    */
+                                   /* (K <= 512), tiles of <= 128 columns     */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */

@@ -86,6 +86,28 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, con
   return 0;
 }
 
+int encode_tmap_kblocks_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int64_t K,
+                           int64_t rows, int64_t row_stride, uint32_t box_rows, uint32_t box_kb) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return set_error(FRN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const int64_t full = K / 64;
+  const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(full > 0 ? full : 1)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride) * 2, 128};
+  const cuuint32_t box[3] = {64, box_rows,
+                             static_cast<cuuint32_t>(full > 0 && full < box_kb ? full : box_kb)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FRN_ERR_INVALID_ARGUMENT,
+                     "cuTensorMapEncodeTiled failed (%d) for the k-block view of a %lld x %lld "
+                     "tensor",
+                     static_cast<int>(r), static_cast<long long>(rows), static_cast<long long>(K));
+  return 0;
+}
+
 int sm_count(int device) {
   static int cache[kMaxDevices] = {0};
   if (device >= 0 && device < kMaxDevices && cache[device] > 0) return cache[device];
@@ -352,6 +374,12 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
     const int bn = kernel == FRN_KERNEL_XRES_AUTO ? choose_xres_bn(M, N, K, sms / 2)
                                                   : bns[kernel - FRN_KERNEL_XRES_N128];
     return run_fused_linear_xres(p, bn, s);
+  }
+  if (kernel == FRN_KERNEL_PAIR_TS) {
+    if (K > 512)
+      return set_error(FRN_ERR_UNSUPPORTED, "the x-in-TMEM kernel takes K <= 512 (got %lld)",
+                       (long long)K);
+    return run_fused_linear_ts(p, s);
   }
   if (kernel == FRN_KERNEL_DECODE) {
     if (M > 128)

@@ -69,6 +69,14 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, con
                    int64_t inner, int64_t outer, int64_t row_stride, uint32_t box_inner,
                    uint32_t box_outer, CUtensorMapSwizzle swizzle);
 
+// 3-D view of a 16-bit [rows x K] row-major tensor as (64 elements, rows,
+// K/64 whole k-blocks) with the 128-byte swizzle: a box of box_rows x box_kb
+// k-blocks lands in shared memory as box_kb consecutive [box_rows x 128 B]
+// blocks, exactly as box_kb 2-D [64 x box_rows] loads would.  Only whole
+// k-blocks are addressable (a ragged last k-block needs the 2-D map).
+int encode_tmap_kblocks_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int64_t K,
+                           int64_t rows, int64_t row_stride, uint32_t box_rows, uint32_t box_kb);
+
 int sm_count(int device);
 // Bound on every in-kernel wait (FRN_WAIT_TIMEOUT_MS, default 2000 ms).
 uint64_t wait_timeout_ns();
@@ -87,6 +95,8 @@ int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s)
 // x-resident pair kernel for K <= 512 (frn_fused_linear_xres.cu).
 int choose_xres_bn(int64_t M, int64_t N, int64_t K, int pairs, bool tile64 = false);
 int run_fused_linear_xres(const LinearProblem& pr, int bn, cudaStream_t s);
+// x-in-TMEM pair kernel for K <= 512 (frn_fused_linear_ts.cu).
+int run_fused_linear_ts(const LinearProblem& pr, cudaStream_t s);
 // SwiGLU on the pair kernel: pr.w = [gate; up] with pr.N = 2 * inter rows;
 // the output has `inter` columns; tiles are 256 x bn output columns.
 int choose_swiglu_bn(int64_t M, int64_t inter, int64_t K, int pairs);

@@ -76,10 +76,10 @@ inline int build_pair_out(const LinearProblem& pr, int64_t n_out, bool half_tail
   return 0;
 }
 
-// Epilogue of one linear pair tile for a warp whose TMEM lane quarter holds
-// rows row_base .. row_base+31 of this CTA's half (taddr points at that
-// quarter of the accumulator): for each 64-column chunk c (the last may be 32
-// wide) with c % chunk_mod == chunk_sel, TMEM -> fp32 -> acc * inv_rms (+ b)
+// Epilogue of one linear pair tile, `width` (<= TILE_N, a multiple of 32)
+// columns wide, for a warp whose TMEM lane quarter holds rows row_base ..
+// row_base+31 of this CTA's half (taddr points at that quarter of the
+// accumulator): for each 64-column chunk c (the last may be 32 wide) with c % chunk_mod == chunk_sel, TMEM -> fp32 -> acc * inv_rms (+ b)
 // -> one rounding -> 128B-swizzled [32 x 64] smem block (double-buffered at
 // stg + (nst % 2) * 4 KB) -> TMA tensor store through the output part's map,
 // which also clips rows >= M and columns >= N.  After its last TMEM read the
@@ -92,16 +92,17 @@ __device__ __forceinline__ void pair_store_linear_tile(uint8_t* stg, uint32_t la
                                                        const PairOut& outm, uint32_t& nst,
                                                        bool release_acc,
                                                        uint32_t tmem_empty_remote,
-                                                       int chunk_mod = 1, int chunk_sel = 0) {
-  constexpr int NCHUNK = (TILE_N + 63) / 64;
-  constexpr bool HALF_TAIL = TILE_N % 64 != 0;
+                                                       int chunk_mod = 1, int chunk_sel = 0,
+                                                       int width = TILE_N) {
+  const int nchunk = (width + 63) / 64;
+  const bool half_tail = width % 64 != 0;
   constexpr int STG_BYTES = 32 * 128;
   const bool has_bias = bias != nullptr;
-  int c_last = NCHUNK - 1;  // this warp's last chunk
+  int c_last = nchunk - 1;  // this warp's last chunk
   while (c_last % chunk_mod != chunk_sel) --c_last;
 #pragma unroll 1
-  for (int c = chunk_sel; c < NCHUNK; c += chunk_mod, ++nst) {
-    const bool half = HALF_TAIL && c == NCHUNK - 1;
+  for (int c = chunk_sel; c < nchunk; c += chunk_mod, ++nst) {
+    const bool half = half_tail && c == nchunk - 1;
     const int col0 = n0 + c * 64;
     uint4 bv[8];
     if (has_bias) {

@@ -45,6 +45,7 @@ FRN_KERNEL_XRES_N192 = 16
 FRN_KERNEL_XRES_N224 = 17
 FRN_KERNEL_XRES_N256 = 18
 FRN_KERNEL_XRES_AUTO = 19
+FRN_KERNEL_PAIR_TS = 20
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {
