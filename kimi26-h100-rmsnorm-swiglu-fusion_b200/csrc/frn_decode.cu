@@ -21,8 +21,14 @@
 // the reduction combines the two halves into 64 output columns.
 //
 // Roles: warps 0-3 epilogue (TMEM lanes -> partial buffer) and reduction,
-// warps 4-7 TMA producers (W / x over even / odd stages), warp 8 MMA issuer +
-// TMEM owner, warps 9-12 RMS (thread t sums x[t, k-range]^2 from x stages).
+// warps 4-7 TMA producers (W / x over even / odd stages), warps 8 and 13 MMA
+// issuers of the even / odd k-blocks into two accumulators (warp 8 also owns
+// TMEM), warps 9-12 RMS (thread t sums x[t, k-range]^2 from x stages).
+//
+// Two issuers: a chain of MMAs into one accumulator completes one 128 x MP x
+// 16 MMA only every ~115-190 clocks however small MP is, so with one chain
+// the MMAs fell behind the weight stream and finished ~2 us after the last
+// k-block arrived; two independent chains (summed in the epilogue) keep up.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -80,20 +86,20 @@ struct DecodeCfg {
   static constexpr int W_BYTES = BM * BK * 2;
   static constexpr int X_BYTES = MP * BK * 2;
   static constexpr int STAGE_TX = W_BYTES + X_BYTES;
-  static constexpr uint32_t TMEM_COLS = MP < 32 ? 32u : static_cast<uint32_t>(MP);
+  static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32u : static_cast<uint32_t>(2 * MP);
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
   static constexpr int PART_BYTES = MP * BM * 4;  // fp32 partial D, [token][w row]
   static constexpr int PIPE_BYTES = STAGES * (W_BYTES + X_BYTES);
   static constexpr int OFF_SS = (PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES);
   static constexpr int OFF_BAR = OFF_SS + 128 * 4;
-  static constexpr int NUM_BARS = 2 * STAGES + 2;
+  static constexpr int NUM_BARS = 2 * STAGES + 3;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
-  // warps 4-7: producers (W | x) x (even | odd stages); 8: MMA; 9-12: RMS
-  static constexpr int WARP_PROD0 = 4, WARP_MMA = 8, WARP_RMS0 = 9;
-  static constexpr int THREADS = 32 * 13;
-  static_assert(STAGES % 2 == 0, "stages are split between two producers per operand");
+  // warps 4-7: producers (W | x) x (even | odd stages); 8, 13: MMA; 9-12: RMS
+  static constexpr int WARP_PROD0 = 4, WARP_MMA = 8, WARP_RMS0 = 9, WARP_MMA1 = 13;
+  static constexpr int THREADS = 32 * 14;
+  static_assert(STAGES % 2 == 0, "stages alternate between two producers and two issuers");
   static_assert(MP % 16 == 0 && MP >= 16 && MP <= 128, "MP");
   static_assert(X_BYTES % 1024 == 0, "x stages must stay 1024-aligned");
   // The partial buffer may only overlap the W stages (read by the MMA alone),
@@ -117,7 +123,7 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* empty = full + STAGES;
   uint64_t* tmem_full = empty + STAGES;
-  uint64_t* drain = tmem_full + 1;
+  uint64_t* drain = tmem_full + 1;  // [issuer]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile uint32_t* abort_flag = tmem_slot + 1;
   float* part = reinterpret_cast<float*>(smem);  // reuses the pipeline buffers
@@ -142,8 +148,9 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
       mbar_init(&full[s], 2);       // W producer + x producer arrive with tx
       mbar_init(&empty[s], 1 + 4);  // MMA commit + 4 RMS warps
     }
-    mbar_init(tmem_full, 1);
-    mbar_init(drain, 1);
+    mbar_init(tmem_full, 2);  // one commit per issuer
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0u;
     fence_mbarrier_init();
   }
@@ -205,27 +212,31 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
     }
-  } else if (warp == C::WARP_MMA) {
+  } else if (warp == C::WARP_MMA || warp == C::WARP_MMA1) {
+    // Issuer pp: k-blocks pp, pp + 2, ... (stages of parity pp) into
+    // accumulator pp at TMEM column pp * MP.
+    const int pp = warp == C::WARP_MMA ? 0 : 1;
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(Elem16<T>::kUmmaFormat, C::BM, MP);
-      uint32_t stage = 0, phase = 0;
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(pp * MP);
       bool ok = true;
-      for (int i = 0; i < nkb; ++i) {
+      for (int i = pp; i < nkb; i += 2) {
+        const int stage = i % STAGES;
+        const uint32_t phase = static_cast<uint32_t>(i / STAGES) & 1u;
         if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
         tc_fence_after();
         const uint32_t w_addr = smem_addr(smem + C::OFF_W + stage * C::W_BYTES);
         const uint32_t x_addr = smem_addr(smem + C::OFF_X + stage * C::X_BYTES);
 #pragma unroll
         for (int k = 0; k < C::BK / 16; ++k)
-          umma_f16_ss(tmem_base, make_smem_desc_k_sw128(w_addr + k * 32),
-                      make_smem_desc_k_sw128(x_addr + k * 32), idesc, (i > 0 || k > 0) ? 1u : 0u);
+          umma_f16_ss(d_tmem, make_smem_desc_k_sw128(w_addr + k * 32),
+                      make_smem_desc_k_sw128(x_addr + k * 32), idesc, (i > pp || k > 0) ? 1u : 0u);
         umma_commit(&empty[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
       if (ok) umma_commit(tmem_full);
-      umma_commit(drain);
+      umma_commit(&drain[pp]);
       uint32_t zero = 0;
-      mbar_wait(drain, 0, &zero, to);
+      mbar_wait(&drain[pp], 0, &zero, to);
     }
   } else if (warp >= C::WARP_RMS0) {
     // Thread t sums x[t, k-range]^2 straight from the x stages.
@@ -261,13 +272,17 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((q * 32u) << 16);
       const int wrow = static_cast<int>(q * 32 + lane);
+      const bool two = nkb >= 2;  // the odd issuer had k-blocks to accumulate
 #pragma unroll 1
       for (int c = 0; c < MP / 16; ++c) {
-        uint32_t v[16];
+        uint32_t v[16], v1[16];
         tmem_ld_32x32b_x16(taddr + c * 16, v);
+        if (two) tmem_ld_32x32b_x16(taddr + MP + c * 16, v1);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) part[(c * 16 + e) * C::BM + wrow] = __uint_as_float(v[e]);
+        for (int e = 0; e < 16; ++e)
+          part[(c * 16 + e) * C::BM + wrow] =
+              __uint_as_float(v[e]) + (two ? __uint_as_float(v1[e]) : 0.f);
       }
     }
   }
