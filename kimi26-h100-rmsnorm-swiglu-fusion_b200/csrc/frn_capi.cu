@@ -108,6 +108,24 @@ int encode_tmap_kblocks_3d(CUtensorMap* map, CUtensorMapDataType dt, const void*
   return 0;
 }
 
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                   const uint64_t (&dims)[3], const uint64_t (&strides)[2],
+                   const uint32_t (&box)[3], CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return set_error(FRN_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  const cuuint64_t st[2] = {strides[0], strides[1]};
+  const cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), d, st, bx, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d) for a 3-D view",
+                     static_cast<int>(r));
+  return 0;
+}
+
 int sm_count(int device) {
   static int cache[kMaxDevices] = {0};
   if (device >= 0 && device < kMaxDevices && cache[device] > 0) return cache[device];

@@ -77,6 +77,12 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, con
 int encode_tmap_kblocks_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int64_t K,
                            int64_t rows, int64_t row_stride, uint32_t box_rows, uint32_t box_kb);
 
+// Generic 3-D tiled map (dims and box innermost first, byte strides of dims
+// 1 and 2), OOB reads as zero.
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                   const uint64_t (&dims)[3], const uint64_t (&strides)[2],
+                   const uint32_t (&box)[3], CUtensorMapSwizzle swizzle);
+
 int sm_count(int device);
 // Bound on every in-kernel wait (FRN_WAIT_TIMEOUT_MS, default 2000 ms).
 uint64_t wait_timeout_ns();
@@ -126,6 +132,12 @@ size_t gqa_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t S);
 int gqa_choose_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t T, int sms,
                       size_t workspace_bytes);
 int run_gqa_decode(const GqaProblem& g, int splits, cudaStream_t s);
+// Tensor-core first pass (frn_gqa_decode_mma.cu) for bf16 / fp16, D 64 or
+// 128, G <= 8; run_gqa_decode picks it when it applies.  The split count may
+// come down (never up) to keep every CTA resident.
+bool gqa_mma_supported(const GqaProblem& g);
+int run_gqa_decode_mma(const GqaProblem& g, int splits, cudaStream_t s);
+int run_gqa_merge(const GqaProblem& g, int S, cudaStream_t s);
 // Static device scratch of the allocation-free GQA entry point.
 int gqa_noalloc_scratch(int dev, void** ptr);
 size_t gqa_noalloc_scratch_bytes();

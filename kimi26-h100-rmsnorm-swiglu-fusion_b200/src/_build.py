@@ -40,6 +40,7 @@ CU_SOURCES = [
     "frn_fused_linear_w8.cu",
     "frn_normalize.cu",
     "frn_gqa_decode.cu",
+    "frn_gqa_decode_mma.cu",
 ]
 HEADERS = ["frn_ptx.cuh", "frn_internal.h"]
 

@@ -22,6 +22,13 @@ SHAPES = [
     (4, 8, 8, 64, 777),
     (3, 16, 2, 64, 2048),
     (1, 64, 8, 128, 8192),
+    # tensor-core path edges: context not a multiple of the 64-token stage,
+    # shorter than a stage, G = 2, 3, 7, many batches
+    (8, 32, 8, 128, 333),
+    (2, 8, 4, 64, 64),
+    (1, 12, 4, 128, 65),
+    (16, 32, 8, 128, 512),
+    (2, 28, 4, 128, 1000),
 ]
 
 
