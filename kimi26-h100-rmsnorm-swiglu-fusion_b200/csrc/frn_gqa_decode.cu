@@ -368,37 +368,6 @@ int gqa_noalloc_scratch(int dev, void** ptr) {
 
 size_t gqa_noalloc_scratch_bytes() { return kGqaNoAllocScratchBytes; }
 
-// Second pass alone, for the tensor-core first pass: the split partials are
-// in g.workspace in the layout GqaParams describes.
-int run_gqa_merge(const GqaProblem& g, int S, cudaStream_t stream) {
-  GqaParams p{};
-  p.out = g.out;
-  p.B = static_cast<int32_t>(g.B);
-  p.Hq = static_cast<int32_t>(g.Hq);
-  p.Hkv = static_cast<int32_t>(g.Hkv);
-  p.T = static_cast<int32_t>(g.T);
-  p.G = static_cast<int32_t>(g.Hq / g.Hkv);
-  p.S = S;
-  float* ws = static_cast<float*>(g.workspace);
-  p.ws_acc = ws;
-  p.ws_ml = ws + static_cast<int64_t>(g.B) * g.Hq * S * g.D;
-  const unsigned rows = static_cast<unsigned>(g.B * g.Hq), threads = static_cast<unsigned>(g.D);
-  switch (g.dtype) {
-    case FRN_DTYPE_BF16:
-      gqa_decode_merge_kernel<__nv_bfloat16><<<rows, threads, 0, stream>>>(p, static_cast<int>(g.D));
-      break;
-    case FRN_DTYPE_F16:
-      gqa_decode_merge_kernel<__half><<<rows, threads, 0, stream>>>(p, static_cast<int>(g.D));
-      break;
-    default:
-      gqa_decode_merge_kernel<float><<<rows, threads, 0, stream>>>(p, static_cast<int>(g.D));
-      break;
-  }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error("launch gqa_decode_merge", e);
-  return 0;
-}
-
 int run_gqa_decode(const GqaProblem& g, int splits, cudaStream_t s) {
   if (gqa_mma_supported(g)) return run_gqa_decode_mma(g, splits, s);
   switch (g.dtype) {

@@ -18,9 +18,12 @@
 // boxes with the 128-byte swizzle) into a 3-slot ring; warps 0-3 each take 16
 // tokens of every stage: ldmatrix (K as the B operand of S, V transposed as
 // the B operand of O), MMAs, online softmax in base 2.  Tokens past the
-// split's end read as -inf scores.  The four warps merge in shared memory and
-// write the output (one split) or the split's (acc, max, sum) for
-// gqa_decode_merge_kernel.
+// split's end read as -inf scores.  The four warps merge in shared memory;
+// with one split the CTA writes the output, otherwise the S <= 8 splits of a
+// (batch, KV head) are one thread-block cluster: each CTA leaves its (acc,
+// max, sum) in shared memory and, after a cluster barrier, combines a 1/S
+// slice of the outputs from all S CTAs through distributed shared memory (no
+// workspace, no second launch).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -37,8 +40,6 @@ namespace frn {
 struct GqaMmaParams {
   const void* q;
   void* out;
-  float* ws_acc;  // [B*Hq*S*D] split partial accumulators (S > 1)
-  float* ws_ml;   // [B*Hq*S*2] split (max, sum)
   int32_t B, Hq, Hkv, T, G, S, tokens_per_split;
   float qscale;  // scale * log2(e)
   uint64_t timeout_ns;
@@ -55,8 +56,10 @@ struct GqaMmaCfg {
   static constexpr int OFF_BAR = kGqaRing * STAGE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 2 * kGqaRing * 8 + 16 + 1024;
   static constexpr int THREADS = 192;
-  // The warps' merge reuses the ring: [4 warps][8 heads][D] acc + m + l.
-  static_assert(4 * 8 * D * 4 + 2 * 4 * 8 * 4 <= OFF_BAR, "merge buffers fit in the ring");
+  // The merges reuse the ring: [4 warps][8 heads][D] acc + m + l, then the
+  // CTA's [8][D] acc + [8] max + [8] sum for the cluster merge.
+  static constexpr int MERGE_FLOATS = 4 * 8 * D + 2 * 4 * 8;
+  static_assert((MERGE_FLOATS + 8 * D + 16) * 4 <= OFF_BAR, "merge buffers fit in the ring");
 };
 
 template <typename T>
@@ -106,7 +109,13 @@ __device__ __forceinline__ __half to_out<__half>(float v) {
   return __float2half_rn(v);
 }
 
-// Barrier among the four compute warps (the loader warps have left).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Barrier among the four compute warps (the loader warps skip the merge).
 __device__ __forceinline__ void bar_sync_compute() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
@@ -153,6 +162,7 @@ __global__ void __launch_bounds__(GqaMmaCfg<D>::THREADS, 2)
 
   if (warp >= 4) {
     // Loader: warp 4 streams K, warp 5 streams V (HALVES boxes per stage).
+    // It takes part in the cluster barriers at the end, nothing else.
     if (lane == 0) {
       const bool is_v = warp == 5;
       const CUtensorMap* m = is_v ? &tmap_v : &tmap_k;
@@ -172,9 +182,7 @@ __global__ void __launch_bounds__(GqaMmaCfg<D>::THREADS, 2)
                       row0 + i * kGqaStageTokens);
       }
     }
-    return;
-  }
-
+  } else {
   // ---- compute warps: fragment coordinates
   const int g = lane >> 2, tq = lane & 3;
   // Q as the A operand of S: rows = heads (g < G real), k = head dims.
@@ -301,13 +309,45 @@ __global__ void __launch_bounds__(GqaMmaCfg<D>::THREADS, 2)
     if (p.S == 1) {
       static_cast<T*>(p.out)[row * D + d] = to_out<T>(num / den);
     } else {
-      const int64_t slot = row * p.S + split;
-      p.ws_acc[slot * D + d] = num;
+      float* cta_acc = sm_acc + C::MERGE_FLOATS;  // [8][D]
+      float* cta_ml = cta_acc + 8 * D;            // [8] max, [8] sum
+      cta_acc[gg * D + d] = num;
       if (d == 0) {
-        p.ws_ml[slot * 2] = mx;
-        p.ws_ml[slot * 2 + 1] = den;
+        cta_ml[gg] = mx;
+        cta_ml[8 + gg] = den;
       }
     }
+  }
+  }  // compute warps
+
+  if (p.S > 1) {
+    // Cluster merge: CTA `split` (its rank) combines outputs [lo, hi) of the
+    // G*D from all S CTAs, in rank order.
+    cluster_sync_all();
+    if (warp < 4 && !*abort_flag) {
+      const uint32_t acc_local = smem_addr(smem) + C::MERGE_FLOATS * 4;
+      const uint32_t ml_local = acc_local + 8 * D * 4;
+      const int total = G * D, chunk = (total + p.S - 1) / p.S;
+      const int lo = split * chunk, hi = min(total, lo + chunk);
+      for (int idx = lo + static_cast<int>(threadIdx.x); idx < hi; idx += 128) {
+        const int gg = idx / D, d = idx % D;
+        float ms[8], mx = -FLT_MAX;
+        for (int r = 0; r < p.S; ++r) {
+          ms[r] = ld_dsmem_f32(mapa_shared(ml_local + gg * 4, r));
+          mx = fmaxf(mx, ms[r]);
+        }
+        float num = 0.f, den = 0.f;
+        for (int r = 0; r < p.S; ++r) {
+          const float f = exp2f(ms[r] - mx);
+          num = fmaf(ld_dsmem_f32(mapa_shared(acc_local + (gg * D + d) * 4, r)), f, num);
+          den = fmaf(ld_dsmem_f32(mapa_shared(ml_local + (8 + gg) * 4, r)), f, den);
+        }
+        const int64_t row = static_cast<int64_t>(b) * p.Hq + kvh * G + gg;
+        static_cast<T*>(p.out)[row * D + d] = to_out<T>(num / den);
+      }
+    }
+    // No CTA leaves while a peer may still read its shared memory.
+    cluster_sync_relaxed();
   }
 }
 
@@ -339,6 +379,7 @@ static int launch_gqa_mma(const GqaProblem& g, int S, cudaStream_t stream) {
   if (S > fit) S = fit > 1 ? static_cast<int>(fit) : 1;
   const int64_t by_len = (g.T + kGqaStageTokens - 1) / kGqaStageTokens;
   if (S > by_len) S = static_cast<int>(by_len);
+  if (S > 8) S = 8;  // the splits of a (batch, KV head) form one portable cluster
   if (S < 1) S = 1;
 
   const CUtensorMapDataType dt = Elem16<T>::kTmaType;
@@ -366,15 +407,21 @@ static int launch_gqa_mma(const GqaProblem& g, int S, cudaStream_t stream) {
   p.tokens_per_split = static_cast<int32_t>((g.T + S - 1) / S);
   p.qscale = g.scale * 1.4426950408889634f;  // log2(e): the softmax runs in base 2
   p.timeout_ns = wait_timeout_ns();
-  float* ws = static_cast<float*>(g.workspace);
-  p.ws_acc = S > 1 ? ws : nullptr;
-  p.ws_ml = S > 1 ? ws + static_cast<int64_t>(g.B) * g.Hq * S * D : nullptr;
-  const dim3 grid(static_cast<unsigned>(g.Hkv), static_cast<unsigned>(g.B),
-                  static_cast<unsigned>(S));
-  kern<<<grid, C::THREADS, C::SMEM_BYTES, stream>>>(tk, tv, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(g.Hkv), static_cast<unsigned>(g.B),
+                     static_cast<unsigned>(S));
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 1;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = static_cast<unsigned>(S);
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
   if (e != cudaSuccess) return set_cuda_error("launch gqa_decode_mma", e);
-  if (S > 1) return run_gqa_merge(g, S, stream);
   return 0;
 }
 

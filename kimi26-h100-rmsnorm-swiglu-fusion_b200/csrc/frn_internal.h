@@ -132,12 +132,12 @@ size_t gqa_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int64_t S);
 int gqa_choose_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t T, int sms,
                       size_t workspace_bytes);
 int run_gqa_decode(const GqaProblem& g, int splits, cudaStream_t s);
-// Tensor-core first pass (frn_gqa_decode_mma.cu) for bf16 / fp16, D 64 or
-// 128, G <= 8; run_gqa_decode picks it when it applies.  The split count may
-// come down (never up) to keep every CTA resident.
+// Tensor-core kernel (frn_gqa_decode_mma.cu) for bf16 / fp16, D 64 or 128,
+// G <= 8, splits merged inside a cluster (no workspace used); run_gqa_decode
+// picks it when it applies.  The split count may come down (never up) to keep
+// every CTA resident and the cluster portable (<= 8).
 bool gqa_mma_supported(const GqaProblem& g);
 int run_gqa_decode_mma(const GqaProblem& g, int splits, cudaStream_t s);
-int run_gqa_merge(const GqaProblem& g, int S, cudaStream_t s);
 // Static device scratch of the allocation-free GQA entry point.
 int gqa_noalloc_scratch(int dev, void** ptr);
 size_t gqa_noalloc_scratch_bytes();
