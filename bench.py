@@ -65,6 +65,8 @@ def parse_args():
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-config sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--gqa-only", action="store_true",
+                    help="time only the GQA decode-attention workload (one JSON line; for profiling)")
     return ap.parse_args()
 
 
@@ -581,6 +583,13 @@ def sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps):
 
 def main():
     args = parse_args()
+    if args.gqa_only:
+        import torch
+        from src.load_cuda import denominator_cuda
+        hbm_gbs, _, _ = read_peaks()
+        print(json.dumps({"gqa_decode_llama": sweep_gqa(
+            denominator_cuda, torch.device("cuda"), hbm_gbs, 40)}))
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
