@@ -14,16 +14,21 @@
 // and scale are applied once, to the fp32 accumulator.
 //
 // Layout: the SM-pair (cta_group::2) kernel of frn_fused_linear_pair.cu with
-// one more role.  Per stage and CTA: x tile [128 x 64] bf16 (TMA, completes on
-// the even CTA's `full`), int8 W half-tile [BN/2 x 64] (TMA, 64B-swizzled,
-// completes on this CTA's `qfull`), and the bf16 copy of that half-tile that
-// the converter warps write in the UMMA 128B-swizzled K-major layout and then
-// announce on the even CTA's `conv` barrier (its own converter arrives and
-// expects 4 bytes, which the odd CTA's converter sends with st.async).
+// one more role and two rings.  The main ring's stage holds, per CTA, the x
+// tile [128 x 64] bf16 (TMA, completes on the even CTA's `full`) and the bf16
+// copy of this CTA's W half-tile, which the converter warps write in the UMMA
+// 128B-swizzled K-major layout and announce on the even CTA's `conv` barrier
+// (its own converter arrives and expects 4 bytes, which the odd CTA's
+// converter sends with st.async).  The int8 half-tiles [BN/2 x 64] (TMA,
+// 64B-swizzled) stream through a ring of their own, QST slots deep, so they
+// are in shared memory well before a converter needs them: the conversion,
+// not the int8 load latency, is what the main ring waits for.
 //
-// Roles (each CTA): warps 0-3 epilogue, warps 4-5 producers (x and int8 W of
-// even / odd stages), warp 6 MMA (even CTA) + TMEM owner, warps 7-10 RMS,
-// warps 11-14 converters (warp = stage mod 4, lane = W rows of the half-tile).
+// Roles (each CTA): warps 0-3 epilogue, warps 4 and 15 x producers (even /
+// odd k-blocks of the sequence: one thread completes a tensor TMA only every
+// few hundred clocks), warp 5 int8 producer, warp 6 MMA (even CTA) + TMEM
+// owner, warps 7-10 RMS, warps 11-14 converters (k-block sequence mod 4,
+// lane = W rows of the half-tile).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -45,7 +50,7 @@ struct W8Params {
   uint64_t timeout_ns;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int QST>
 struct W8Cfg {
   static constexpr int BM = 128;
   static constexpr int BK = 64;
@@ -59,20 +64,19 @@ struct W8Cfg {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_Q = OFF_B + STAGES * B_BYTES;
-  static constexpr int OFF_STG = OFF_Q + STAGES * Q_BYTES;
+  static constexpr int OFF_STG = OFF_Q + QST * Q_BYTES;
   static constexpr int OFF_RMS = OFF_STG + 4 * 2 * STG_BYTES;
   static constexpr int OFF_SCL = OFF_RMS + 2 * BM * 4;  // per epilogue warp: the tile's scale[n]
   static constexpr int OFF_BAR = OFF_SCL + 4 * BN * 4;
   static constexpr int NCHUNK = (BN + 63) / 64;  // epilogue chunks of 64 columns
   static constexpr bool HALF_TAIL = BN % 64 != 0;
-  static constexpr int NUM_BARS = 5 * STAGES + 9;
+  static constexpr int NUM_BARS = 4 * STAGES + 2 * QST + 9;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   static constexpr int EPI_WARPS = 4, RMS_WARPS = 4, CONV_WARPS = 4;
-  static constexpr int WARP_PROD0 = 4, WARP_MMA = 6, WARP_RMS0 = 7, WARP_CONV0 = 11;
-  static constexpr int THREADS = 32 * 15;
-  // Producers take stages by parity and converters k-blocks by sequence, so
-  // any ring depth works; an odd one leaves one producer a stage more.
+  static constexpr int WARP_XLOAD = 4, WARP_QLOAD = 5, WARP_MMA = 6, WARP_RMS0 = 7,
+                       WARP_CONV0 = 11, WARP_XLOAD1 = 15;
+  static constexpr int THREADS = 32 * 16;
   static_assert(B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "stage buffers must stay aligned");
   static_assert(OFF_STG % 1024 == 0, "staging blocks must be 1024-aligned for the 128B swizzle");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
@@ -116,24 +120,25 @@ __device__ __forceinline__ void widen_s8x4<__half>(uint32_t w, uint32_t& o01, ui
       : "r"(h01), "r"(h23), "r"(c));
 }
 
-template <typename T, int BN, int STAGES>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::THREADS, 1)
+template <typename T, int BN, int STAGES, int QST>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QST>::THREADS, 1)
     fused_rmsnorm_linear_w8_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                    const __grid_constant__ CUtensorMap tmap_q,
                                    const __grid_constant__ CUtensorMap tmap_out,
                                    const __grid_constant__ CUtensorMap tmap_out_half,
                                    const W8Params p) {
-  using C = W8Cfg<BN, STAGES>;
+  using C = W8Cfg<BN, STAGES, QST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);  // even CTA: x of both CTAs
-  uint64_t* qfull = full + STAGES;                                 // this CTA's int8 tile
-  uint64_t* conv = qfull + STAGES;                                 // even CTA: bf16 W ready
+  uint64_t* conv = full + STAGES;                                  // even CTA: bf16 W ready
   uint64_t* mma_done = conv + STAGES;
   uint64_t* empty = mma_done + STAGES;
-  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* qfull = empty + STAGES;   // [QST] this CTA's int8 tile landed
+  uint64_t* qempty = qfull + QST;     // [QST] its converter is done with it
+  uint64_t* tmem_full = qempty + QST;
   uint64_t* tmem_empty = tmem_full + 2;
   uint64_t* rms_full = tmem_empty + 2;
   uint64_t* rms_empty = rms_full + 2;
@@ -148,17 +153,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
   const uint32_t pair = blockIdx.x >> 1;
   const uint32_t num_pairs = gridDim.x >> 1;
 
-  if (warp == C::WARP_PROD0 && lane == 0) {
+  if (warp == C::WARP_XLOAD && lane == 0) {
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_q);
     prefetch_tmap(&tmap_out);
     if (C::HALF_TAIL) prefetch_tmap(&tmap_out_half);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&qfull[s], 1);
       mbar_init(&conv[s], 1);  // even CTA's converter arrives; odd CTA's sends 4 tx bytes
       mbar_init(&mma_done[s], 1);
       mbar_init(&empty[s], C::RMS_WARPS);
+    }
+    for (int s = 0; s < QST; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
@@ -196,31 +204,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
   // still orders all of its global accesses after this whole grid.
   griddep_launch_dependents();
 
-  if (warp == C::WARP_PROD0 || warp == C::WARP_PROD0 + 1) {
-    // Producer p issues the x tile and the int8 W half-tile of the stages
-    // with s % 2 == p.
+  if (warp == C::WARP_XLOAD || warp == C::WARP_XLOAD1) {
+    // x tiles into the main ring (both CTAs' halves complete on the even
+    // CTA's `full`, armed by the even CTA); this thread takes the k-blocks
+    // of the sequence with i % 2 == sel.
+    if (lane == 0) {
+      const uint32_t sel = warp == C::WARP_XLOAD ? 0u : 1u;
+      griddep_wait();
+      uint32_t i = 0;
+      bool ok = true;
+      for (int t = t_begin; t < t_end && ok; ++t) {
+        const int m0 = (t / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
+        for (int kb = 0; kb < nkb; ++kb, ++i) {
+          if ((i & 1u) != sel) continue;
+          const uint32_t s = i % STAGES, ph = (i / STAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, to)) { ok = false; break; }
+          const uint32_t leader_full = mapa_shared(smem_addr(&full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], C::PAIR_A_TX);
+          tma_load_2d_pair(smem + C::OFF_A + s * C::A_BYTES, &tmap_x, leader_full, kb * C::BK,
+                           m0);
+        }
+      }
+    }
+  } else if (warp == C::WARP_QLOAD) {
+    // int8 half-tiles into their own ring, as far ahead as its QST slots go.
     if (lane == 0) {
       griddep_wait();
-      const uint32_t parity_sel = warp - C::WARP_PROD0;
-      uint32_t stage = 0, phase = 0;
-      for (int t = t_begin; t < t_end; ++t) {
-        const int m0 = (t / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
+      uint32_t i = 0;
+      bool ok = true;
+      for (int t = t_begin; t < t_end && ok; ++t) {
         const int n0 = (t % p.num_n_blocks) * BN + rank * C::BN_HALF;
-        bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
-          if ((stage & 1u) == parity_sel) {
-            if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, to)) { ok = false; break; }
-            const uint32_t leader_full = mapa_shared(smem_addr(&full[stage]), 0);
-            if (rank == 0) mbar_arrive_expect_tx(&full[stage], C::PAIR_A_TX);
-            tma_load_2d_pair(smem + C::OFF_A + stage * C::A_BYTES, &tmap_x, leader_full,
-                             kb * C::BK, m0);
-            mbar_arrive_expect_tx(&qfull[stage], C::Q_BYTES);
-            tma_load_2d(smem + C::OFF_Q + stage * C::Q_BYTES, &tmap_q, &qfull[stage], kb * C::BK,
-                        n0);
-          }
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        for (int kb = 0; kb < nkb; ++kb, ++i) {
+          const uint32_t qs = i % QST, qph = (i / QST) & 1u;
+          if (!mbar_wait(&qempty[qs], qph ^ 1u, abort_flag, to)) { ok = false; break; }
+          mbar_arrive_expect_tx(&qfull[qs], C::Q_BYTES);
+          tma_load_2d(smem + C::OFF_Q + qs * C::Q_BYTES, &tmap_q, &qfull[qs], kb * C::BK, n0);
         }
-        if (!ok) break;
       }
     }
   } else if (warp == C::WARP_MMA) {
@@ -269,47 +288,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES>::T
     const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
     const uint32_t leader_sink = mapa_shared(smem_addr(tmem_slot + 2), 0);
     const uint32_t q0 = smem_addr(smem + C::OFF_Q), b0 = smem_addr(smem + C::OFF_B);
-    uint32_t stage = 0, phase = 0, seq = 0;
-    bool ok = true;
-    for (int t = t_begin; t < t_end && ok; ++t) {
-      for (int kb = 0; kb < nkb; ++kb, ++seq) {
-        if (seq % C::CONV_WARPS == cw) {
-          if (!mbar_wait(&qfull[stage], phase, abort_flag, to)) { ok = false; break; }
-          const uint32_t qs = q0 + stage * C::Q_BYTES, bs = b0 + stage * C::B_BYTES;
+    const uint32_t total = static_cast<uint32_t>((t_end - t_begin) * nkb);
+    for (uint32_t i = cw; i < total; i += C::CONV_WARPS) {
+      const uint32_t qs = i % QST, qph = (i / QST) & 1u;
+      const uint32_t stage = i % STAGES, phase = (i / STAGES) & 1u;
+      // The int8 tile has landed, and the main slot's previous MMA is done
+      // (its RMS warps released it).
+      if (!mbar_wait(&qfull[qs], qph, abort_flag, to)) break;
+      if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, to)) break;
+      const uint32_t qsa = q0 + qs * C::Q_BYTES, bs = b0 + stage * C::B_BYTES;
 #pragma unroll 2
-          for (uint32_t j = lane; j < static_cast<uint32_t>(C::BN_HALF); j += 32) {
-            // int8 row j: 64 bytes, 64B-swizzled (16-byte chunk c at c ^ ((j >> 1) & 3));
-            // bf16 row j: 128 bytes, 128B-swizzled (chunk c at c ^ (j & 7)).
-            uint4 w[4];
+      for (uint32_t j = lane; j < static_cast<uint32_t>(C::BN_HALF); j += 32) {
+        // int8 row j: 64 bytes, 64B-swizzled (16-byte chunk c at c ^ ((j >> 1) & 3));
+        // bf16 row j: 128 bytes, 128B-swizzled (chunk c at c ^ (j & 7)).
+        uint4 w[4];
 #pragma unroll
-            for (uint32_t c = 0; c < 4; ++c)
-              w[c] = ld_shared_v4(qs + j * 64 + ((c ^ ((j >> 1) & 3u)) << 4));
+        for (uint32_t c = 0; c < 4; ++c)
+          w[c] = ld_shared_v4(qsa + j * 64 + ((c ^ ((j >> 1) & 3u)) << 4));
 #pragma unroll
-            for (uint32_t c = 0; c < 4; ++c) {
-              uint32_t o[8];
-              widen_s8x4<T>(w[c].x, o[0], o[1]);
-              widen_s8x4<T>(w[c].y, o[2], o[3]);
-              widen_s8x4<T>(w[c].z, o[4], o[5]);
-              widen_s8x4<T>(w[c].w, o[6], o[7]);
-              st_shared_v4(bs + j * 128 + (((2 * c) ^ (j & 7u)) << 4), o[0], o[1], o[2], o[3]);
-              st_shared_v4(bs + j * 128 + (((2 * c + 1) ^ (j & 7u)) << 4), o[4], o[5], o[6], o[7]);
-            }
-          }
-          // The tensor cores (async proxy) read what was just written.  The
-          // even CTA arrives locally and expects 4 bytes; the odd CTA sends
-          // them with st.async, whose complete_tx on the even CTA's barrier is
-          // a cluster-scope release that does not stall this warp (a
-          // releasing remote arrive costs a few hundred cycles here).
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (rank == 0)
-              mbar_arrive_expect_tx(&conv[stage], 4u);
-            else
-              st_async_complete_tx(leader_sink, 1u, leader_conv0 + stage * 8);
-          }
+        for (uint32_t c = 0; c < 4; ++c) {
+          uint32_t o[8];
+          widen_s8x4<T>(w[c].x, o[0], o[1]);
+          widen_s8x4<T>(w[c].y, o[2], o[3]);
+          widen_s8x4<T>(w[c].z, o[4], o[5]);
+          widen_s8x4<T>(w[c].w, o[6], o[7]);
+          st_shared_v4(bs + j * 128 + (((2 * c) ^ (j & 7u)) << 4), o[0], o[1], o[2], o[3]);
+          st_shared_v4(bs + j * 128 + (((2 * c + 1) ^ (j & 7u)) << 4), o[4], o[5], o[6], o[7]);
         }
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      // The tensor cores (async proxy) read what was just written.  The even
+      // CTA arrives locally and expects 4 bytes; the odd CTA sends them with
+      // st.async, whose complete_tx on the even CTA's barrier is a
+      // cluster-scope release that does not stall this warp (a releasing
+      // remote arrive costs a few hundred cycles here).
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&qempty[qs]);
+        if (rank == 0)
+          mbar_arrive_expect_tx(&conv[stage], 4u);
+        else
+          st_async_complete_tx(leader_sink, 1u, leader_conv0 + stage * 8);
       }
     }
   } else if (warp >= C::WARP_RMS0) {
@@ -499,10 +518,10 @@ int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws
 
 // ------------------------------------------------------------------ host side
 
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, int QST>
 static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
-  using C = W8Cfg<BN, STAGES>;
-  auto kern = fused_rmsnorm_linear_w8_kernel<T, BN, STAGES>;
+  using C = W8Cfg<BN, STAGES, QST>;
+  auto kern = fused_rmsnorm_linear_w8_kernel<T, BN, STAGES, QST>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
   static int max_pairs[kMaxDevices] = {};
@@ -580,8 +599,8 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
 }
 
 // Tile width for the int8 kernel: the fewest tensor-core columns on the
-// busiest pair, ceil(tiles / pairs) * bn (ties to the wider tile); widths up to
-// 224 get a five-stage ring, 256 fits only four.
+// busiest pair, ceil(tiles / pairs) * bn (ties to the wider tile); 256 leaves
+// room for only six int8 slots instead of eight.
 static int choose_w8_bn(int64_t M, int64_t N, int pairs) {
   static const int cands[] = {256, 224, 192, 128};
   const int64_t mb = (M + 255) / 256;
@@ -599,10 +618,10 @@ static int choose_w8_bn(int64_t M, int64_t N, int pairs) {
 template <typename T>
 static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
   switch (choose_w8_bn(pr.M, pr.N, sm_count(0) / 2)) {
-    case 256: return launch_w8<T, 256, 4>(pr, s);
-    case 224: return launch_w8<T, 224, 5>(pr, s);
-    case 192: return launch_w8<T, 192, 5>(pr, s);
-    default: return launch_w8<T, 128, 6>(pr, s);
+    case 256: return launch_w8<T, 256, 4, 6>(pr, s);
+    case 224: return launch_w8<T, 224, 4, 8>(pr, s);
+    case 192: return launch_w8<T, 192, 4, 8>(pr, s);
+    default: return launch_w8<T, 128, 6, 8>(pr, s);
   }
 }
 
