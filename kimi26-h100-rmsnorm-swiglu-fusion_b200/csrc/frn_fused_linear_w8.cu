@@ -619,8 +619,8 @@ template <typename T>
 static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
   switch (choose_w8_bn(pr.M, pr.N, sm_count(0) / 2)) {
     case 256: return launch_w8<T, 256, 4, 6>(pr, s);
-    case 224: return launch_w8<T, 224, 4, 8>(pr, s);
-    case 192: return launch_w8<T, 192, 4, 8>(pr, s);
+    case 224: return launch_w8<T, 224, 5, 5>(pr, s);
+    case 192: return launch_w8<T, 192, 5, 6>(pr, s);
     default: return launch_w8<T, 128, 6, 8>(pr, s);
   }
 }
