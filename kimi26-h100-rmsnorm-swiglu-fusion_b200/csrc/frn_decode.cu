@@ -55,19 +55,6 @@ struct DecodeParams {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ float2 ld_shared_cluster_f32x2(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr)
-               : "memory");
-  return v;
-}
-
 template <int MP, int STAGES>
 struct DecodeCfg {
   static constexpr int BM = 128;  // W rows per tile
@@ -78,11 +65,20 @@ struct DecodeCfg {
   static constexpr uint32_t TMEM_COLS = 2 * MP < 32 ? 32u : static_cast<uint32_t>(2 * MP);
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
-  static constexpr int PART_BYTES = MP * BM * 4;  // fp32 partial D, [token][w row]
   static constexpr int PIPE_BYTES = STAGES * (W_BYTES + X_BYTES);
-  static constexpr int OFF_SS = (PIPE_BYTES > PART_BYTES ? PIPE_BYTES : PART_BYTES);
-  static constexpr int OFF_BAR = OFF_SS + 128 * 4;
+  // Receive buffer of the cluster reduction: fp32 [source rank][owned token
+  // slot][W row].  An owner holds ceil(MP / S) token slots per source rank,
+  // S * ceil(MP / S) <= MP + 7 for S <= 8.  Its own space when that fits
+  // beside the pipeline, else it reuses the W stages (after every CTA of the
+  // cluster has finished its MMAs).
+  static constexpr int RECV_BYTES = (MP + 8) * BM * 4;
+  static constexpr int SS_BYTES = (MP + 8) * 4;  // [source rank][owned token slot] sums of x^2
   static constexpr int NUM_BARS = 2 * STAGES + 3;
+  static constexpr int TAIL_BYTES = SS_BYTES + NUM_BARS * 8 + 16 + 1024;
+  static constexpr bool RECV_OWN = PIPE_BYTES + RECV_BYTES + TAIL_BYTES <= 232448;
+  static constexpr int OFF_RECV = RECV_OWN ? PIPE_BYTES : 0;
+  static constexpr int OFF_SS = RECV_OWN ? PIPE_BYTES + RECV_BYTES : PIPE_BYTES;
+  static constexpr int OFF_BAR = OFF_SS + SS_BYTES;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   // warps 4-7: producers (W | x) x (even | odd stages); 8, 13: MMA; 9-12: RMS
@@ -91,9 +87,9 @@ struct DecodeCfg {
   static_assert(STAGES % 2 == 0, "stages alternate between two producers and two issuers");
   static_assert(MP % 16 == 0 && MP >= 16 && MP <= 128, "MP");
   static_assert(X_BYTES % 1024 == 0, "x stages must stay 1024-aligned");
-  // The partial buffer may only overlap the W stages (read by the MMA alone),
-  // never the x stages, which RMS warps can still be reading.
-  static_assert(PART_BYTES <= STAGES * W_BYTES, "partial buffer overlaps the x stages");
+  static_assert(RECV_OWN || RECV_BYTES <= STAGES * W_BYTES,
+                "a shared receive buffer may only overlap the W stages");
+  static_assert(OFF_BAR % 8 == 0, "mbarriers need 8-byte alignment");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
 
@@ -115,8 +111,8 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   uint64_t* drain = tmem_full + 1;  // [issuer]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile uint32_t* abort_flag = tmem_slot + 1;
-  float* part = reinterpret_cast<float*>(smem);  // reuses the pipeline buffers
-  float* ssq = reinterpret_cast<float*>(smem + C::OFF_SS);
+  float* recv = reinterpret_cast<float*>(smem + C::OFF_RECV);
+  float* ss_recv = reinterpret_cast<float*>(smem + C::OFF_SS);
 
   const uint32_t warp = warp_id_in_cta();
   const uint32_t lane = threadIdx.x & 31u;
@@ -151,6 +147,15 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Cluster rendezvous A guards the first write into a peer's shared memory.
+  // With a receive buffer of its own, a CTA is ready for its peers' writes
+  // once it has started, so it arrives now; otherwise it arrives once its
+  // pipeline buffers are no longer read (below).
+  if (C::RECV_OWN) cluster_arrive_relaxed();
+  bool acc_ready = false;
+  float rms_ss[MP / 16];  // RMS warps: per-token partial sums of x^2 of this lane's chunk
+#pragma unroll
+  for (int i = 0; i < MP / 16; ++i) rms_ss[i] = 0.f;
   // Let the next kernel in the stream get scheduled now: its CTAs take SMs as
   // ours retire and run their set-up while we finish; its griddepcontrol.wait
   // still orders all of its global accesses after this whole grid.
@@ -228,55 +233,102 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
       mbar_wait(&drain[pp], 0, &zero, to);
     }
   } else if (warp >= C::WARP_RMS0) {
-    // Thread t sums x[t, k-range]^2 straight from the x stages.
-    const int t = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;
+    // The x stage's MP rows x 8 16-byte chunks are spread over the 128
+    // threads: thread tid takes chunk tid % 8 of tokens i * 16 + tid / 8, so
+    // every thread has work at any MP (one warp doing all of a small batch
+    // fell ~1 us behind the stream).  The 8 chunk sums of a token are
+    // combined with shuffles after the loop.
+    const int tid = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;
+    const uint32_t q = static_cast<uint32_t>(tid) & 7u;
+    const int g = tid >> 3;
     uint32_t stage = 0, phase = 0;
-    float ss0 = 0.f, ss1 = 0.f;
     for (int i = 0; i < nkb; ++i) {
       if (!mbar_wait(&full[stage], phase, abort_flag, to)) break;
-      if (t < MP) {
-        const uint32_t row = smem_addr(smem + C::OFF_X + stage * C::X_BYTES) + t * 128;
+      const uint32_t xs = smem_addr(smem + C::OFF_X + stage * C::X_BYTES);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint4 v = ld_shared_v4(row + ((q ^ (t & 7)) << 4));
-          const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
-          const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
-          ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
-          ss0 = fmaf(f1.x, f1.x, ss0); ss1 = fmaf(f1.y, f1.y, ss1);
-          ss0 = fmaf(f2.x, f2.x, ss0); ss1 = fmaf(f2.y, f2.y, ss1);
-          ss0 = fmaf(f3.x, f3.x, ss0); ss1 = fmaf(f3.y, f3.y, ss1);
-        }
+      for (int j = 0; j < MP / 16; ++j) {
+        const uint32_t t = static_cast<uint32_t>(j * 16 + g);
+        const uint4 v = ld_shared_v4(xs + t * 128u + ((q ^ (t & 7u)) << 4));
+        const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
+        const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
+        float a = rms_ss[j];
+        a = fmaf(f0.x, f0.x, a); a = fmaf(f0.y, f0.y, a);
+        a = fmaf(f1.x, f1.x, a); a = fmaf(f1.y, f1.y, a);
+        a = fmaf(f2.x, f2.x, a); a = fmaf(f2.y, f2.y, a);
+        a = fmaf(f3.x, f3.x, a); a = fmaf(f3.y, f3.y, a);
+        rms_ss[j] = a;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
       if (++stage == STAGES) { stage = 0; phase ^= 1u; }
     }
-    // Published after the cluster barrier below, once the pipeline is idle.
-    if (t < MP) ssq[t] = ss0 + ss1;
+#pragma unroll
+    for (int j = 0; j < MP / 16; ++j) {
+      float a = rms_ss[j];
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      a += __shfl_xor_sync(0xffffffffu, a, 4);
+      rms_ss[j] = a;
+    }
   } else {
-    // Epilogue warps 0-3: accumulator lanes -> partial buffer [token][w row].
-    // The pipeline buffers are reused, so wait until every MMA is done.
-    const uint32_t q = warp;
-    if (mbar_wait(tmem_full, 0, abort_flag, to)) {
+    // Epilogue warps 0-3: wait until every MMA of this CTA is done.
+    acc_ready = mbar_wait(tmem_full, 0, abort_flag, to);
+  }
+
+  // Rendezvous A: every CTA of the cluster can take its peers' writes.
+  __syncwarp();
+  tc_fence_before();
+  if (!C::RECV_OWN) cluster_arrive_release();  // after this CTA's last use of its W stages
+  cluster_wait();
+
+  // Token t belongs to CTA t % S (slot t / S).  Each CTA writes its partial
+  // D^T row of every token, and the RMS warps its partial sum of x^2, into
+  // the owner's receive buffer at [this rank][slot], so that the reduction
+  // below reads only local shared memory (remote loads cost a long round
+  // trip each; remote stores do not wait).
+  const int t_end = p.M < MP ? p.M : MP;
+  const int towns = (MP + S - 1) / S;  // token slots per source rank
+  if (warp < 4) {
+    if (acc_ready) {
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((q * 32u) << 16);
-      const int wrow = static_cast<int>(q * 32 + lane);
+      const uint32_t taddr = tmem_base + ((warp * 32u) << 16);
+      const uint32_t wrow = warp * 32u + lane;
       const bool two = nkb >= 2;  // the odd issuer had k-blocks to accumulate
+      const uint32_t mine =
+          smem_addr(recv) + ((rank * static_cast<uint32_t>(towns)) * C::BM + wrow) * 4u;
+      int o = 0, tl = 0;  // owner and slot of token c * 16 + e
 #pragma unroll 1
-      for (int c = 0; c < MP / 16; ++c) {
+      for (int c = 0; c < MP / 16 && c * 16 < t_end; ++c) {
         uint32_t v[16], v1[16];
         tmem_ld_32x32b_x16(taddr + c * 16, v);
         if (two) tmem_ld_32x32b_x16(taddr + MP + c * 16, v1);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          part[(c * 16 + e) * C::BM + wrow] =
-              __uint_as_float(v[e]) + (two ? __uint_as_float(v1[e]) : 0.f);
+        for (int e = 0; e < 16; ++e) {
+          if (c * 16 + e < t_end)
+            st_shared_cluster_f32(
+                mapa_shared(mine + static_cast<uint32_t>(tl) * (C::BM * 4u), static_cast<uint32_t>(o)),
+                __uint_as_float(v[e]) + (two ? __uint_as_float(v1[e]) : 0.f));
+          if (++o == S) { o = 0; ++tl; }
+        }
+      }
+    }
+  } else if (warp >= C::WARP_RMS0 && warp < C::WARP_RMS0 + 4) {
+    const int tid = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;
+    if ((tid & 7) == 0) {
+#pragma unroll
+      for (int j = 0; j < MP / 16; ++j) {
+        const int t = j * 16 + (tid >> 3);
+        if (t < t_end)
+          st_shared_cluster_f32(
+              mapa_shared(smem_addr(ss_recv) + static_cast<uint32_t>(rank * towns + t / S) * 4u,
+                          static_cast<uint32_t>(t % S)),
+              rms_ss[j]);
       }
     }
   }
 
-  // All partials (and x^2 sums) of the cluster are in shared memory.
+  // Rendezvous B: every write into this CTA's receive buffer has landed.
   __syncwarp();
   tc_fence_before();
   cluster_sync_all();
@@ -309,14 +361,11 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         bu1 = bv.y;
       }
     }
-    const uint32_t part_local = smem_addr(part);
-    const uint32_t ssq_local = smem_addr(ssq);
-    // Tokens in batches of kBatch: every distributed-shared-memory load of a
-    // batch is issued before any is consumed (remote loads are slow).
+    // Owned tokens t = rank + S * tl, tl < n_own; thread group tsub takes
+    // tl = tsub, tsub + LANES, ...
     constexpr int kBatch = 4;
-    const int t_first = static_cast<int>(rank) + S * tsub;
-    const int t_end = p.M < MP ? p.M : MP;
-    for (int t0 = t_first; t0 < t_end; t0 += LANES * S * kBatch) {
+    const int n_own = t_end > static_cast<int>(rank) ? (t_end - static_cast<int>(rank) + S - 1) / S : 0;
+    for (int tl0 = tsub; tl0 < n_own; tl0 += LANES * kBatch) {
       float2 acc[kBatch], accu[kBatch];
       float ss[kBatch];
 #pragma unroll
@@ -326,17 +375,16 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         ss[j] = 0.f;
       }
       for (int s = 0; s < S; ++s) {  // fixed rank order: deterministic sums
-        const uint32_t part_s = mapa_shared(part_local, s);
-        const uint32_t ssq_s = mapa_shared(ssq_local, s);
         float2 v[kBatch], u[kBatch];
         float q[kBatch];
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-          const int t = t0 + j * LANES * S;
-          const int tc = t < t_end ? t : t_first;  // clamp: loads stay in bounds
-          v[j] = ld_shared_cluster_f32x2(part_s + (tc * C::BM + pr) * 4);
-          if (SWIGLU) u[j] = ld_shared_cluster_f32x2(part_s + (tc * C::BM + 64 + pr) * 4);
-          q[j] = ld_shared_cluster_f32(ssq_s + tc * 4);
+          const int tl = tl0 + j * LANES;
+          const int tc = tl < n_own ? tl : tl0;  // clamp: loads stay on written slots
+          const float* slot = recv + (s * towns + tc) * C::BM;
+          v[j] = *reinterpret_cast<const float2*>(slot + pr);
+          if (SWIGLU) u[j] = *reinterpret_cast<const float2*>(slot + 64 + pr);
+          q[j] = ss_recv[s * towns + tc];
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
@@ -351,8 +399,9 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        const int t = t0 + j * LANES * S;
-        if (t < t_end && col_ok) {
+        const int tl = tl0 + j * LANES;
+        const int t = static_cast<int>(rank) + S * tl;
+        if (tl < n_own && col_ok) {
           const float r = rsqrtf(ss[j] / static_cast<float>(p.K) + p.eps);
           T* o = obase + static_cast<int64_t>(t) * ostride;
           float y0 = acc[j].x * r + b0, y1 = acc[j].y * r + b1;
@@ -366,11 +415,9 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     }
   }
 
-  // Nobody leaves while a peer may still read its shared memory.  The peers'
-  // remote reads have all returned (their values are already stored), so
-  // the rendezvous needs no release.
+  // No CTA touches a peer's shared memory after rendezvous B, so CTAs leave
+  // without another cluster barrier.
   __syncwarp();
-  cluster_sync_relaxed();
   if (*abort_flag) __nanosleep(20000);
   if (warp == C::WARP_MMA) {
     tc_fence_after();

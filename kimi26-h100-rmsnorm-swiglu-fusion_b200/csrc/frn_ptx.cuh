@@ -324,6 +324,24 @@ __device__ __forceinline__ void cluster_sync_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// The two halves of a cluster rendezvous, for a thread that has other work
+// between announcing it is ready and needing everyone else to be.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// 4-byte store into the shared memory of any CTA of the cluster
+// (`cluster_addr` from mapa_shared).
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
 // 2-D tiled TMA load for a CTA pair: data lands in this CTA's smem, the
 // transaction bytes are signalled on `bar_cluster_addr`, which may be the
 // mbarrier of either CTA of the pair.
