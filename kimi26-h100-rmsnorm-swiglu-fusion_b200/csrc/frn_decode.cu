@@ -333,83 +333,89 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   tc_fence_before();
   cluster_sync_all();
 
-  if (warp < 4 && !*abort_flag) {
-    // CTA `rank` reduces tokens rank, rank+S, ...: TPT threads per token, each
-    // owning output columns pr, pr+1 of the tile (W rows pr, pr+1, and for
-    // SwiGLU also the up rows 64+pr, 65+pr); 128 / TPT tokens in flight.
+  if (warp < 8 && !*abort_flag) {
+    // CTA `rank` reduces its owned tokens t = rank + S * tl, tl < n_own, with
+    // warps 0-7 (the epilogue and producer warps, idle by now).  First
+    // inv_rms[t] = rsqrt(sum_s ss_s[t] / K + eps), once per token, into slot
+    // [0][tl] of the x^2 receive buffer (a thread reads only its own token's
+    // slots); then TPT threads per token, each owning 4 output columns of the
+    // tile (W rows pc .. pc+3, and for SwiGLU also the up rows 64+pc ..).
+    constexpr int RT = 256;                   // reducing threads
+    constexpr int OUTC = SWIGLU ? 64 : 128;   // output columns per tile
+    constexpr int TPT = OUTC / 4;             // threads per token
+    constexpr int LANES = RT / TPT;           // tokens in flight
+    constexpr int kBatch = 2;
+    const int tid = static_cast<int>(threadIdx.x);
+    const int n_own = t_end > static_cast<int>(rank) ? (t_end - static_cast<int>(rank) + S - 1) / S : 0;
+    const uint32_t recv_a = smem_addr(recv), ss_a = smem_addr(ss_recv);
+    // Kernel parameters the loops need, in registers.
+    const float kf = static_cast<float>(p.K), eps = p.eps;
+    for (int tl = tid; tl < n_own; tl += RT) {
+      float ss = 0.f;
+      for (int s = 0; s < S; ++s)  // fixed rank order: deterministic sums
+        ss += ld_shared_f32(ss_a + static_cast<uint32_t>(s * towns + tl) * 4u);
+      ss_recv[tl] = rsqrtf(ss / kf + eps);
+    }
+    named_bar_sync(1, RT);
     griddep_wait();
-    constexpr int TPT = SWIGLU ? 32 : 64;
-    constexpr int LANES = 128 / TPT;
-    const int pr = static_cast<int>(threadIdx.x % TPT) * 2;
-    const int tsub = static_cast<int>(threadIdx.x / TPT);
-    const bool col_ok = n0 + pr < p.N;
-    int pi = 0;  // output part of columns n0 + pr, n0 + pr + 1 (parts are 8-column multiples)
-    while (pi + 1 < p.nparts && n0 + pr >= p.part_col0[pi + 1]) ++pi;
-    T* const obase = static_cast<T*>(p.part_out[pi]) + (n0 + pr - p.part_col0[pi]);
+    const int pc = (tid % TPT) * 4;
+    const int tsub = tid / TPT;
+    const bool col_ok = n0 + pc < p.N;  // N and part widths are multiples of 8
+    int pi = 0;  // output part of columns n0 + pc .. n0 + pc + 3
+    while (pi + 1 < p.nparts && n0 + pc >= p.part_col0[pi + 1]) ++pi;
+    T* const obase = static_cast<T*>(p.part_out[pi]) + (n0 + pc - p.part_col0[pi]);
     const int64_t ostride = p.part_stride[pi];
-    const bool has_bias = p.bias != nullptr;
-    float b0 = 0.f, b1 = 0.f, bu0 = 0.f, bu1 = 0.f;
-    if (has_bias && col_ok) {
+    float bg[4] = {0.f, 0.f, 0.f, 0.f}, bu[4] = {0.f, 0.f, 0.f, 0.f};
+    if (p.bias != nullptr && col_ok) {
       const T* bias = static_cast<const T*>(p.bias);
-      const float2 bb = pair_to_float2<T>(*reinterpret_cast<const uint32_t*>(bias + n0 + pr));
-      b0 = bb.x;
-      b1 = bb.y;
+      const uint2 b = *reinterpret_cast<const uint2*>(bias + n0 + pc);
+      const float2 b01 = pair_to_float2<T>(b.x), b23 = pair_to_float2<T>(b.y);
+      bg[0] = b01.x; bg[1] = b01.y; bg[2] = b23.x; bg[3] = b23.y;
       if (SWIGLU) {
-        const float2 bv = pair_to_float2<T>(
-            *reinterpret_cast<const uint32_t*>(bias + p.up_row0 + n0 + pr));
-        bu0 = bv.x;
-        bu1 = bv.y;
+        const uint2 c = *reinterpret_cast<const uint2*>(bias + p.up_row0 + n0 + pc);
+        const float2 c01 = pair_to_float2<T>(c.x), c23 = pair_to_float2<T>(c.y);
+        bu[0] = c01.x; bu[1] = c01.y; bu[2] = c23.x; bu[3] = c23.y;
       }
     }
-    // Owned tokens t = rank + S * tl, tl < n_own; thread group tsub takes
-    // tl = tsub, tsub + LANES, ...
-    constexpr int kBatch = 4;
-    const int n_own = t_end > static_cast<int>(rank) ? (t_end - static_cast<int>(rank) + S - 1) / S : 0;
     for (int tl0 = tsub; tl0 < n_own; tl0 += LANES * kBatch) {
-      float2 acc[kBatch], accu[kBatch];
-      float ss[kBatch];
+      float4 acc[kBatch], accu[kBatch];
+      float r[kBatch];
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        acc[j] = make_float2(0.f, 0.f);
-        accu[j] = make_float2(0.f, 0.f);
-        ss[j] = 0.f;
+        acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        accu[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int tl = tl0 + j * LANES;
+        r[j] = ld_shared_f32(ss_a + static_cast<uint32_t>(tl < n_own ? tl : tl0) * 4u);
       }
       for (int s = 0; s < S; ++s) {  // fixed rank order: deterministic sums
-        float2 v[kBatch], u[kBatch];
-        float q[kBatch];
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
           const int tl = tl0 + j * LANES;
           const int tc = tl < n_own ? tl : tl0;  // clamp: loads stay on written slots
-          const float* slot = recv + (s * towns + tc) * C::BM;
-          v[j] = *reinterpret_cast<const float2*>(slot + pr);
-          if (SWIGLU) u[j] = *reinterpret_cast<const float2*>(slot + 64 + pr);
-          q[j] = ss_recv[s * towns + tc];
-        }
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-          acc[j].x += v[j].x;
-          acc[j].y += v[j].y;
+          const uint32_t slot = recv_a + static_cast<uint32_t>((s * towns + tc) * C::BM + pc) * 4u;
+          const float4 v = ld_shared_v4f(slot);
+          acc[j].x += v.x; acc[j].y += v.y; acc[j].z += v.z; acc[j].w += v.w;
           if (SWIGLU) {
-            accu[j].x += u[j].x;
-            accu[j].y += u[j].y;
+            const float4 u = ld_shared_v4f(slot + 64 * 4);
+            accu[j].x += u.x; accu[j].y += u.y; accu[j].z += u.z; accu[j].w += u.w;
           }
-          ss[j] += q[j];
         }
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
         const int tl = tl0 + j * LANES;
-        const int t = static_cast<int>(rank) + S * tl;
         if (tl < n_own && col_ok) {
-          const float r = rsqrtf(ss[j] / static_cast<float>(p.K) + p.eps);
-          T* o = obase + static_cast<int64_t>(t) * ostride;
-          float y0 = acc[j].x * r + b0, y1 = acc[j].y * r + b1;
+          const int t = static_cast<int>(rank) + S * tl;
+          float y[4] = {acc[j].x * r[j] + bg[0], acc[j].y * r[j] + bg[1],
+                        acc[j].z * r[j] + bg[2], acc[j].w * r[j] + bg[3]};
           if (SWIGLU) {
-            y0 = __fdividef(y0, 1.0f + __expf(-y0)) * (accu[j].x * r + bu0);
-            y1 = __fdividef(y1, 1.0f + __expf(-y1)) * (accu[j].y * r + bu1);
+            const float u[4] = {accu[j].x, accu[j].y, accu[j].z, accu[j].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              y[e] = __fdividef(y[e], 1.0f + __expf(-y[e])) * (u[e] * r[j] + bu[e]);
           }
-          *reinterpret_cast<uint32_t*>(o) = float2_to_pair<T>(y0, y1);
+          *reinterpret_cast<uint2*>(obase + static_cast<int64_t>(t) * ostride) =
+              make_uint2(float2_to_pair<T>(y[0], y[1]), float2_to_pair<T>(y[2], y[3]));
         }
       }
     }
