@@ -149,9 +149,13 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
   // Cluster rendezvous A guards the first write into a peer's shared memory.
   // With a receive buffer of its own, a CTA is ready for its peers' writes
-  // once it has started, so it arrives now; otherwise it arrives once its
-  // pipeline buffers are no longer read (below).
-  if (C::RECV_OWN) cluster_arrive_relaxed();
+  // once it has started, so A is taken now (a warp that took it only after
+  // its mainloop work waited ~0.4 us there); otherwise every CTA arrives once
+  // its pipeline buffers are no longer read (below).
+  if (C::RECV_OWN) {
+    cluster_arrive_relaxed();
+    cluster_wait();
+  }
   bool acc_ready = false;
   float rms_ss[MP / 16];  // RMS warps: per-token partial sums of x^2 of this lane's chunk
 #pragma unroll
@@ -275,11 +279,14 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
     acc_ready = mbar_wait(tmem_full, 0, abort_flag, to);
   }
 
-  // Rendezvous A: every CTA of the cluster can take its peers' writes.
+  // Rendezvous A (shared receive buffer): every CTA of the cluster is done
+  // with its W stages and can take its peers' writes.
   __syncwarp();
   tc_fence_before();
-  if (!C::RECV_OWN) cluster_arrive_release();  // after this CTA's last use of its W stages
-  cluster_wait();
+  if (!C::RECV_OWN) {
+    cluster_arrive_release();  // after this CTA's last use of its W stages
+    cluster_wait();
+  }
 
   // Token t belongs to CTA t % S (slot t / S).  Each CTA writes its partial
   // D^T row of every token, and the RMS warps its partial sum of x^2, into
@@ -305,10 +312,11 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          if (c * 16 + e < t_end)
-            st_shared_cluster_f32(
-                mapa_shared(mine + static_cast<uint32_t>(tl) * (C::BM * 4u), static_cast<uint32_t>(o)),
-                __uint_as_float(v[e]) + (two ? __uint_as_float(v1[e]) : 0.f));
+          if (c * 16 + e < t_end) {
+            const uint32_t a = mine + static_cast<uint32_t>(tl) * (C::BM * 4u);
+            const float val = __uint_as_float(v[e]) + (two ? __uint_as_float(v1[e]) : 0.f);
+            st_shared_cluster_f32(mapa_shared(a, static_cast<uint32_t>(o)), val);
+          }
           if (++o == S) { o = 0; ++tl; }
         }
       }
