@@ -210,6 +210,9 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
       }
     }
+    // The producer warps help the epilogue warps move the accumulators out.
+    __syncwarp();
+    acc_ready = mbar_wait(tmem_full, 0, abort_flag, to);
   } else if (warp == C::WARP_MMA || warp == C::WARP_MMA1) {
     // Issuer pp: k-blocks pp, pp + 2, ... (stages of parity pp) into
     // accumulator pp at TMEM column pp * MP.
@@ -295,17 +298,20 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   // trip each; remote stores do not wait).
   const int t_end = p.M < MP ? p.M : MP;
   const int towns = (MP + S - 1) / S;  // token slots per source rank
-  if (warp < 4) {
+  if (warp < 8) {
+    // Warps w and w + 4 share TMEM lane quarter w % 4 (W rows 32 (w % 4) ..)
+    // and take alternate 16-token chunks.
     if (acc_ready) {
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((warp * 32u) << 16);
-      const uint32_t wrow = warp * 32u + lane;
+      const uint32_t quarter = warp & 3u;
+      const uint32_t taddr = tmem_base + ((quarter * 32u) << 16);
+      const uint32_t wrow = quarter * 32u + lane;
       const bool two = nkb >= 2;  // the odd issuer had k-blocks to accumulate
       const uint32_t mine =
           smem_addr(recv) + ((rank * static_cast<uint32_t>(towns)) * C::BM + wrow) * 4u;
-      int o = 0, tl = 0;  // owner and slot of token c * 16 + e
 #pragma unroll 1
-      for (int c = 0; c < MP / 16 && c * 16 < t_end; ++c) {
+      for (int c = static_cast<int>(warp >> 2); c < MP / 16 && c * 16 < t_end; c += 2) {
+        int o = (c * 16) % S, tl = (c * 16) / S;  // owner and slot of token c * 16 + e
         uint32_t v[16], v1[16];
         tmem_ld_32x32b_x16(taddr + c * 16, v);
         if (two) tmem_ld_32x32b_x16(taddr + MP + c * 16, v1);
