@@ -20,10 +20,11 @@
 // the B operand of O), MMAs, online softmax in base 2.  Tokens past the
 // split's end read as -inf scores.  The four warps merge in shared memory;
 // with one split the CTA writes the output, otherwise the S <= 8 splits of a
-// (batch, KV head) are one thread-block cluster: each CTA leaves its (acc,
-// max, sum) in shared memory and, after a cluster barrier, combines a 1/S
-// slice of the outputs from all S CTAs through distributed shared memory (no
-// workspace, no second launch).
+// (batch, KV head) are one thread-block cluster: CTA r owns a 1/S slice of
+// the G*D outputs, every CTA pushes its (acc, max, sum) for each slice into
+// the owner's receive buffer with st.shared::cluster, and after one cluster
+// barrier each owner combines its slice from local shared memory in rank
+// order (no workspace, no second launch, no remote loads).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -54,12 +55,18 @@ struct GqaMmaCfg {
   static constexpr int HALF_BYTES = kGqaStageTokens * 128;  // [64 tokens x 64 d]
   static constexpr int STAGE_BYTES = 2 * HALVES * HALF_BYTES;  // K then V
   static constexpr int OFF_BAR = kGqaRing * STAGE_BYTES;
-  static constexpr int SMEM_BYTES = OFF_BAR + 2 * kGqaRing * 8 + 16 + 1024;
+  // Cluster-merge receive buffer, a space of its own (peers may write it
+  // while this CTA still streams): acc [S][ceil(G*D/S)] (<= 8*D + 7 floats)
+  // then max and sum [S][16].
+  static constexpr int OFF_RECV = OFF_BAR + 64;
+  static constexpr int RECV_ACC_FLOATS = 8 * D + 8;
+  static constexpr int RECV_FLOATS = RECV_ACC_FLOATS + 8 * 16;
+  static constexpr int SMEM_BYTES = OFF_RECV + RECV_FLOATS * 4 + 1024;
   static constexpr int THREADS = 192;
-  // The merges reuse the ring: [4 warps][8 heads][D] acc + m + l, then the
-  // CTA's [8][D] acc + [8] max + [8] sum for the cluster merge.
+  // The warp merge reuses the ring: [4 warps][8 heads][D] acc + m + l.
   static constexpr int MERGE_FLOATS = 4 * 8 * D + 2 * 4 * 8;
-  static_assert((MERGE_FLOATS + 8 * D + 16) * 4 <= OFF_BAR, "merge buffers fit in the ring");
+  static_assert(MERGE_FLOATS * 4 <= OFF_BAR, "merge buffers fit in the ring");
+  static_assert(2 * kGqaRing * 8 + 4 <= 64, "barriers and flag fit before the receive buffer");
 };
 
 template <typename T>
@@ -109,12 +116,6 @@ __device__ __forceinline__ __half to_out<__half>(float v) {
   return __float2half_rn(v);
 }
 
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
 // Barrier among the four compute warps (the loader warps skip the merge).
 __device__ __forceinline__ void bar_sync_compute() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -159,6 +160,16 @@ __global__ void __launch_bounds__(GqaMmaCfg<D>::THREADS, 2)
     fence_mbarrier_init();
   }
   __syncthreads();
+  // Peers write this CTA's receive buffer only after this rendezvous (every
+  // CTA of the cluster has started).
+  if (p.S > 1) {
+    cluster_arrive_relaxed();
+    cluster_wait();
+  }
+  // The next grid in the stream may start its set-up now; everything this
+  // grid reads or writes in global memory waits for the previous grid.
+  griddep_launch_dependents();
+  griddep_wait();
 
   if (warp >= 4) {
     // Loader: warp 4 streams K, warp 5 streams V (HALVES boxes per stage).
@@ -309,12 +320,22 @@ __global__ void __launch_bounds__(GqaMmaCfg<D>::THREADS, 2)
     if (p.S == 1) {
       static_cast<T*>(p.out)[row * D + d] = to_out<T>(num / den);
     } else {
-      float* cta_acc = sm_acc + C::MERGE_FLOATS;  // [8][D]
-      float* cta_ml = cta_acc + 8 * D;            // [8] max, [8] sum
-      cta_acc[gg * D + d] = num;
+      // Output idx belongs to CTA idx / chunk; this CTA's (split's) values go
+      // to slot [split][idx % chunk] of its receive buffer, and every owner
+      // gets this CTA's max and sum of head gg.
+      const int chunk = (G * D + p.S - 1) / p.S;
+      const uint32_t recv_a = smem_addr(smem + C::OFF_RECV);
+      const int owner = idx / chunk;
+      st_shared_cluster_f32(
+          mapa_shared(recv_a + static_cast<uint32_t>(split * chunk + idx - owner * chunk) * 4u,
+                      static_cast<uint32_t>(owner)),
+          num);
       if (d == 0) {
-        cta_ml[gg] = mx;
-        cta_ml[8 + gg] = den;
+        const uint32_t ml_a = recv_a + (C::RECV_ACC_FLOATS + split * 16 + gg) * 4;
+        for (int r = 0; r < p.S; ++r) {
+          st_shared_cluster_f32(mapa_shared(ml_a, static_cast<uint32_t>(r)), mx);
+          st_shared_cluster_f32(mapa_shared(ml_a + 8 * 4, static_cast<uint32_t>(r)), den);
+        }
       }
     }
   }
@@ -322,32 +343,32 @@ __global__ void __launch_bounds__(GqaMmaCfg<D>::THREADS, 2)
 
   if (p.S > 1) {
     // Cluster merge: CTA `split` (its rank) combines outputs [lo, hi) of the
-    // G*D from all S CTAs, in rank order.
+    // G*D from all S CTAs, in rank order, out of its own receive buffer.
+    // After this barrier no CTA touches a peer's shared memory, so none
+    // waits for the others before leaving.
     cluster_sync_all();
     if (warp < 4 && !*abort_flag) {
-      const uint32_t acc_local = smem_addr(smem) + C::MERGE_FLOATS * 4;
-      const uint32_t ml_local = acc_local + 8 * D * 4;
+      const float* racc = reinterpret_cast<const float*>(smem + C::OFF_RECV);
+      const float* rml = racc + C::RECV_ACC_FLOATS;  // [S][16]: max [8], sum [8]
       const int total = G * D, chunk = (total + p.S - 1) / p.S;
       const int lo = split * chunk, hi = min(total, lo + chunk);
       for (int idx = lo + static_cast<int>(threadIdx.x); idx < hi; idx += 128) {
         const int gg = idx / D, d = idx % D;
         float ms[8], mx = -FLT_MAX;
         for (int r = 0; r < p.S; ++r) {
-          ms[r] = ld_dsmem_f32(mapa_shared(ml_local + gg * 4, r));
+          ms[r] = rml[r * 16 + gg];
           mx = fmaxf(mx, ms[r]);
         }
         float num = 0.f, den = 0.f;
         for (int r = 0; r < p.S; ++r) {
           const float f = exp2f(ms[r] - mx);
-          num = fmaf(ld_dsmem_f32(mapa_shared(acc_local + (gg * D + d) * 4, r)), f, num);
-          den = fmaf(ld_dsmem_f32(mapa_shared(ml_local + (8 + gg) * 4, r)), f, den);
+          num = fmaf(racc[r * chunk + idx - lo], f, num);
+          den = fmaf(rml[r * 16 + 8 + gg], f, den);
         }
         const int64_t row = static_cast<int64_t>(b) * p.Hq + kvh * G + gg;
         static_cast<T*>(p.out)[row * D + d] = to_out<T>(num / den);
       }
     }
-    // No CTA leaves while a peer may still read its shared memory.
-    cluster_sync_relaxed();
   }
 }
 
@@ -413,13 +434,15 @@ static int launch_gqa_mma(const GqaProblem& g, int S, cudaStream_t stream) {
   cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = 1;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = static_cast<unsigned>(S);
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tk, tv, p);
   if (e != cudaSuccess) return set_cuda_error("launch gqa_decode_mma", e);
   return 0;
