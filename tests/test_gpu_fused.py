@@ -198,6 +198,20 @@ def test_decode_kernel(M, K, N):
     _check(out, x, gamma, W, W_new, b, f"decode M{M} K{K} N{N}")
 
 
+@pytest.mark.parametrize("M", [1, 9, 64, 128])
+@pytest.mark.parametrize("K,N", [(2048, 1024), (1280, 3200), (1792, 2432)])
+def test_decode_kernel_cluster_sizes(M, K, N):
+    """Shapes that ask for k-splits of 8, 5 and 7 CTAs per cluster (the
+    one-wave cap may lower the last two): other owner / slot mappings of the
+    cluster reduction than the Llama-3-8B shape's 2, with the receive buffer
+    in its own space (M <= 64) and over the W stages (M = 128)."""
+    x, gamma, W, W_new, b = _inputs(M, K, N, seed=7 * M + K + N, bias=True)
+    out = capi.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), b.to(DEV), orc.EPS,
+                                    kernel=capi.FRN_KERNEL_DECODE)
+    torch.cuda.synchronize()
+    _check(out, x, gamma, W, W_new, b, f"decode M{M} K{K} N{N}")
+
+
 def test_decode_strided_fp16_and_determinism():
     M, K, N = 24, 4096, 6144
     x, gamma, W, W_new, b = _inputs(M, K, N, seed=31, dtype=torch.float16, bias=True)
