@@ -12,7 +12,9 @@ implementation: if the library cannot be built or loaded, loading raises.
 from __future__ import annotations
 
 import concurrent.futures
+import contextlib
 import ctypes
+import fcntl
 import hashlib
 import importlib.machinery
 import importlib.util
@@ -42,7 +44,7 @@ CU_SOURCES = [
     "frn_gqa_decode.cu",
     "frn_gqa_decode_mma.cu",
 ]
-HEADERS = ["frn_ptx.cuh", "frn_internal.h"]
+HEADERS = ["frn_ptx.cuh", "frn_internal.h", "frn_pair_common.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
@@ -89,14 +91,39 @@ def _lib_inputs():
     return files
 
 
+def _flags_key() -> str:
+    # The include path is absolute; the tree may be copied elsewhere (another
+    # machine, a scratch directory), so the stamp records it relative.
+    return " ".join(f.replace(REPO_DIR, "<repo>") for f in NVCC_FLAGS)
+
+
+@contextlib.contextmanager
+def _build_lock():
+    """Inter-process lock around check-and-build: several ranks of one job
+    import the package at once and must not build (or load a half-written
+    library) concurrently."""
+    os.makedirs(LIB_DIR, exist_ok=True)
+    with open(os.path.join(LIB_DIR, ".build.lock"), "w") as f:
+        fcntl.flock(f, fcntl.LOCK_EX)
+        try:
+            yield
+        finally:
+            fcntl.flock(f, fcntl.LOCK_UN)
+
+
 def library_is_fresh() -> bool:
-    want = _digest(_lib_inputs(), " ".join(NVCC_FLAGS))
+    want = _digest(_lib_inputs(), _flags_key())
     return os.path.exists(LIB_PATH) and _read(LIB_PATH + ".sha256") == want
 
 
 def build_library(force: bool = False, verbose: bool = False) -> str:
     """Compile every .cu for sm_100a and link libfrn_b200.so (in-tree)."""
-    want = _digest(_lib_inputs(), " ".join(NVCC_FLAGS))
+    with _build_lock():
+        return _build_library_locked(force, verbose)
+
+
+def _build_library_locked(force: bool, verbose: bool) -> str:
+    want = _digest(_lib_inputs(), _flags_key())
     if not force and os.path.exists(LIB_PATH) and _read(LIB_PATH + ".sha256") == want:
         return LIB_PATH
     obj_dir = os.path.join(LIB_DIR, "obj")
@@ -117,7 +144,7 @@ def build_library(force: bool = False, verbose: bool = False) -> str:
 
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(CU_SOURCES))) as ex:
         objs = list(ex.map(compile_one, CU_SOURCES))
-    tmp = LIB_PATH + ".tmp"
+    tmp = f"{LIB_PATH}.{os.getpid()}.tmp"
     cmd = [nvcc] + ARCH_FLAGS + ["-rdc=true", "-shared", "-Xlinker", f"-soname={LIB_NAME}",
                                  "-o", tmp] + objs
     r = subprocess.run(cmd, capture_output=True, text=True)
@@ -175,6 +202,13 @@ def build_denominator_cuda(force: bool = False, verbose: bool = False):
     import torch.utils.cpp_extension as ext
 
     load_library()
+    with _build_lock():
+        return _build_denominator_cuda_locked(force, verbose)
+
+
+def _build_denominator_cuda_locked(force: bool, verbose: bool):
+    import torch.utils.cpp_extension as ext
+
     so = _ext_so_path()
     want = _ext_digest()
     if not force and os.path.exists(so) and _read(so + ".sha256") == want:

@@ -80,3 +80,18 @@ def test_normalize_validation():
 
 def test_workspace_query_is_host_only():
     assert capi.workspace_size(capi.FRN_DTYPE_BF16, 512, 12288, 1536) >= 0
+
+
+def test_build_stamp_is_relocatable_and_covers_every_header():
+    """The library's freshness stamp must not depend on where the tree sits
+    (a copy on another machine would otherwise rebuild, and several ranks of
+    one job would rebuild at once), and must cover every header the kernels
+    include."""
+    from src import _build
+
+    assert _build.REPO_DIR not in _build._flags_key()
+    csrc = _build.CSRC_DIR
+    headers = {f for f in os.listdir(csrc) if f.endswith((".cuh", ".h"))}
+    assert headers <= set(_build.HEADERS), headers - set(_build.HEADERS)
+    sources = {f for f in os.listdir(csrc) if f.endswith(".cu")}
+    assert sources == set(_build.CU_SOURCES)
