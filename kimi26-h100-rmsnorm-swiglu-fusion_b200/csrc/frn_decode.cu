@@ -9,21 +9,24 @@
 //             fp32 accumulator sits in TMEM (lane = W row, column = token).
 //   split-K   the CTAs of one thread-block cluster (S <= 8) share a W tile and
 //             each streams 1/S of K, so N/128 * S CTAs cover the SMs.
-//   reduce    each CTA writes its fp32 partial D^T and its partial sum of x^2
-//             per token into its own shared memory; after a cluster barrier,
-//             CTA r reduces tokens t = r, r+S, ... by reading the S partials
-//             through distributed shared memory in rank order (deterministic,
-//             no atomics, no global workspace), applies
-//             inv_rms[t] = rsqrt(sum_s ss_s[t] / K + eps) and b[n], and stores
-//             out[t, n0 .. n0+127] as coalesced rows.
+//   reduce    token t belongs to CTA t % S.  Once its MMAs are done, each
+//             CTA pushes its fp32 partial D^T column of every token, and its
+//             partial sum of x^2, into the owner's receive buffer
+//             (st.shared::cluster; remote stores do not wait, remote loads
+//             would); after one release/acquire cluster barrier each owner
+//             sums its tokens' S partials from local shared memory in rank
+//             order (deterministic, no atomics, no global workspace), applies
+//             inv_rms[t] = rsqrt(sum_s ss_s[t] / K + eps) and b[n], and
+//             stores out[t, n0 .. n0+127] as coalesced rows.
 //
 // SwiGLU variant: a tile is 64 gate rows over the matching 64 up rows, and
 // the reduction combines the two halves into 64 output columns.
 //
-// Roles: warps 0-3 epilogue (TMEM lanes -> partial buffer) and reduction,
-// warps 4-7 TMA producers (W / x over even / odd stages), warps 8 and 13 MMA
-// issuers of the even / odd k-blocks into two accumulators (warp 8 also owns
-// TMEM), warps 9-12 RMS (thread t sums x[t, k-range]^2 from x stages).
+// Roles: warps 0-3 epilogue, warps 4-7 TMA producers (W / x over even / odd
+// stages), warps 8 and 13 MMA issuers of the even / odd k-blocks into two
+// accumulators (warp 8 also owns TMEM), warps 9-12 RMS (x^2 sums from the x
+// stages, 16-byte chunks spread over all 128 threads).  Warps 0-7 then move
+// the accumulators out of TMEM and push them, and reduce the owned tokens.
 //
 // Two issuers: a chain of MMAs into one accumulator completes one 128 x MP x
 // 16 MMA only every ~115-190 clocks however small MP is, so with one chain
