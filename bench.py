@@ -477,7 +477,9 @@ def run_ours(args):
 
 
 def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
-    """µs/call of every BASELINE shape (ours vs the unfused cuBLAS path)."""
+    """µs/call of every BASELINE shape (ours vs the unfused cuBLAS path):
+    cold (rotating sets larger than L2; the roofline fraction uses this) and
+    hot (one set reused, L2-warm where it fits)."""
     import torch
 
     res = {}
@@ -491,11 +493,14 @@ def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
         n = max(rot.S, min(steps, 4 * rot.S))
         t_ours = time_steps(ours, n, rot.S) * 1e3 / n
         t_base = time_steps(base, n, rot.S) * 1e3 / n
+        # Hot: the same set every call, so whatever of it fits stays in L2.
+        t_hot = time_steps(ours[:1], n, rot.S) * 1e3 / n
         fl, by = flops_of(M, K, N), bytes_of(M, K, N)
         roof_us = max(fl / (tflops_peak * 1e12), by / (hbm_gbs * 1e9)) * 1e6
         res[name] = {"us_per_call": round(t_ours, 3), "tflops": round(fl / t_ours / 1e6, 1),
                      "gbs": round(by / t_ours / 1e3, 1),
                      "roofline_us": round(roof_us, 3), "frac_of_roofline": round(roof_us / t_ours, 3),
+                     "us_per_call_hot_l2": round(t_hot, 3),
                      "unfused_cublas_us": round(t_base, 3),
                      "speedup_vs_unfused": round(t_base / t_ours, 3)}
         del rot
