@@ -346,8 +346,10 @@ __global__ void __launch_bounds__(DecodeCfg<MP, STAGES>::THREADS, 1)
   }
 
   // Rendezvous B: every write into this CTA's receive buffer has landed.
+  // Only warps 0-7 read TMEM since rendezvous A; the others' tcgen05 work was
+  // fenced before it.
   __syncwarp();
-  tc_fence_before();
+  if (warp < 8) tc_fence_before();
   cluster_sync_all();
 
   if (warp < 8 && !*abort_flag) {
