@@ -4,6 +4,8 @@
  * Every entry point takes plain device pointers, element strides and sizes,
  * runs asynchronously on the given CUDA stream (NULL = legacy default stream)
  * and returns an FRN_* status.  No entry point synchronises the stream.
+ * Every call works on the caller's current CUDA device (cudaSetDevice): the
+ * pointers and the stream must belong to it.
  * The message of the last failing call on the calling thread is available
  * from frn_last_error().
  *
@@ -61,13 +63,6 @@ extern "C" {
 #define FRN_KERNEL_WIDE_N192   12  /* SM pair, two accumulators: 256x(2*192)  */
 #define FRN_KERNEL_WIDE_N224   13  /* SM pair, two accumulators: 256x(2*224)  */
 #define FRN_KERNEL_WIDE_N256   14  /* SM pair, two accumulators: 256x(2*256)  */
-#define FRN_KERNEL_XRES_N128   15  /* SM pair, x resident in smem (K <= 512)   */
-#define FRN_KERNEL_XRES_N192   16  /* SM pair, x resident, 256x192 tiles       */
-#define FRN_KERNEL_XRES_N224   17  /* SM pair, x resident, 256x224 tiles       */
-#define FRN_KERNEL_XRES_N256   18  /* SM pair, x resident, 256x256 tiles       */
-#define FRN_KERNEL_XRES_AUTO   19  /* SM pair, x resident, width by (M, N, K)  */
-#define FRN_KERNEL_PAIR_TS     20  /* SM pair, x in TMEM as the A operand    */
-                                   /* (K <= 512), tiles of <= 128 columns     */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */
@@ -218,11 +213,20 @@ int frn_fused_rmsnorm_swiglu(int dtype, const void* x, int64_t M, int64_t K,
  * q [batch, num_q_heads, head_dim], k_cache / v_cache [batch, context_len,
  * num_kv_heads, head_dim], out [batch, num_q_heads, head_dim], all contiguous
  * and of `dtype` (fp32 / fp16 / bf16); head_dim 64 or 128; G = num_q_heads /
- * num_kv_heads <= 8.  The context is split across CTAs when `workspace`
- * (frn_gqa_decode_workspace_size bytes) is given; with no workspace each
- * (batch, KV head) is one CTA.  Replaces gqa_decode_v2_cuda / gqa_decode_v3_cuda
+ * num_kv_heads <= 8.  bf16 / fp16 run on the tensor-core kernel, which splits
+ * the context over a thread-block cluster and merges the splits on chip: it
+ * never reads the workspace.  fp32 runs the CUDA-core kernel, whose context
+ * split writes partials to `workspace` (frn_gqa_decode_workspace_size bytes)
+ * for a second merge launch; with no workspace each (batch, KV head) of an
+ * fp32 call is one CTA.  Replaces gqa_decode_v2_cuda / gqa_decode_v3_cuda
  * (reference csrc/gqa_attention_kernel.cu:357-470, bound in
  * csrc/gqa_attention.cpp:45-60), on the caller's stream.
+ *
+ * frn_gqa_decode_workspace_size returns what the fp32 split path needs for
+ * the shape (an upper bound for every dtype; bf16 / fp16 calls may pass no
+ * workspace at all).  With G <= 8 and head_dim <= 128 the split rule keeps it
+ * at or below 3 * SMs * G * (head_dim + 2) * 4 bytes (1.85 MB on a 148-SM
+ * B200).
  */
 size_t frn_gqa_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
                                      int64_t head_dim, int64_t context_len);
@@ -238,14 +242,18 @@ int frn_gqa_decode_attention(int dtype, const void* q, const void* k_cache, cons
  * hosts whose device memory is wholly reserved up front by their own
  * allocator or memory pool, or that forbid cudaMalloc/cudaFree on their
  * decode path -- and so cannot hand the kernel the workspace its context
- * split needs.  The split partials go to a fixed 2 MiB scratch array inside
- * this library (one per device, set up on first use).  A shape that needs
- * more scratch than that (frn_gqa_decode_workspace_size > 2 MiB) is rejected
- * with FRN_ERR_UNSUPPORTED.  Every call shares that one array, so calls whose
- * work overlaps on the GPU (different streams, or no ordering between them)
- * race and corrupt each other's results; issue them in order on one stream.
- * Nothing in the scratch has to start at zero.  Same results as
- * frn_gqa_decode_attention given its full workspace.
+ * split needs.  bf16 / fp16 calls need no scratch (the tensor-core kernel
+ * merges its splits on chip).  An fp32 call parks its split partials in a
+ * fixed 2 MiB scratch array inside this library (one per device; its device
+ * address is looked up on the first fp32 call on that device, so make that
+ * first call before any stream capture).  An fp32 shape needing more scratch
+ * than that is rejected with FRN_ERR_UNSUPPORTED (on a 148-SM B200 no valid
+ * shape does, see frn_gqa_decode_workspace_size).  Every fp32 call shares
+ * that one array, so fp32 calls whose work overlaps on the GPU (different
+ * streams, or no ordering between them) race and corrupt each other's
+ * results; issue them in order on one stream.  Nothing in the scratch has to
+ * start at zero.  Same results as frn_gqa_decode_attention given its full
+ * workspace.
  * No counterpart in the reference.
  */
 int frn_gqa_decode_attention_noalloc(int dtype, const void* q, const void* k_cache,

@@ -311,10 +311,13 @@ int frn_gqa_decode_attention(int dtype, const void* q, const void* k_cache, cons
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
   const size_t ws_bytes = workspace ? workspace_bytes : 0;
-  const int S = gqa_choose_splits(batch, num_q_heads, num_kv_heads, head_dim, context_len,
-                                  sm_count(dev), ws_bytes);
   GqaProblem g{dtype, q, k_cache, v_cache, out, batch, num_q_heads, num_kv_heads, head_dim,
                context_len, scale, workspace, ws_bytes};
+  // The tensor-core kernel merges its splits inside a cluster and never
+  // touches the workspace, so its split count is not bounded by it.
+  const int S = gqa_choose_splits(batch, num_q_heads, num_kv_heads, head_dim, context_len,
+                                  sm_count(dev),
+                                  gqa_mma_supported(g) ? static_cast<size_t>(-1) : ws_bytes);
   return run_gqa_decode(g, S, static_cast<cudaStream_t>(stream));
 }
 
@@ -332,23 +335,27 @@ int frn_gqa_decode_attention_noalloc(int dtype, const void* q, const void* k_cac
     return set_error(FRN_ERR_MISALIGNED, "q, caches and out must be 16-byte aligned");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
-  // Same split count (hence the same scratch need and the same result) as
-  // frn_gqa_decode_attention given its full workspace.
+  // Same split count (hence the same result) as frn_gqa_decode_attention
+  // given its full workspace.
   const int S = gqa_choose_splits(batch, num_q_heads, num_kv_heads, head_dim, context_len,
                                   sm_count(dev), static_cast<size_t>(-1));
+  GqaProblem g{dtype, q, k_cache, v_cache, out, batch, num_q_heads, num_kv_heads, head_dim,
+               context_len, scale, nullptr, 0};
+  // bf16 / fp16 shapes go to the tensor-core kernel, which merges its splits
+  // through cluster shared memory and needs no scratch at all; only the
+  // CUDA-core split + merge path (fp32) parks partials in the static array.
+  if (gqa_mma_supported(g)) return run_gqa_decode(g, S, static_cast<cudaStream_t>(stream));
   const size_t need = gqa_workspace_bytes(batch, num_q_heads, head_dim, S);
   if (need > gqa_noalloc_scratch_bytes())
     return set_error(FRN_ERR_UNSUPPORTED,
                      "GQA decode needs %zu bytes of scratch for this shape; the static scratch "
                      "holds %zu (use frn_gqa_decode_attention with a workspace)",
                      need, gqa_noalloc_scratch_bytes());
-  void* scratch = nullptr;
   if (need > 0) {
-    rc = gqa_noalloc_scratch(dev, &scratch);
+    rc = gqa_noalloc_scratch(dev, &g.workspace);
     if (rc) return rc;
+    g.workspace_bytes = need;
   }
-  GqaProblem g{dtype, q, k_cache, v_cache, out, batch, num_q_heads, num_kv_heads, head_dim,
-               context_len, scale, scratch, need};
   return run_gqa_decode(g, S, static_cast<cudaStream_t>(stream));
 }
 
@@ -383,21 +390,6 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
   if (kernel >= FRN_KERNEL_WIDE_N128 && kernel <= FRN_KERNEL_WIDE_N256) {
     static const int bns[4] = {128, 192, 224, 256};
     return run_fused_linear_pair(p, PairChoice{bns[kernel - FRN_KERNEL_WIDE_N128], 2}, s);
-  }
-  if (kernel >= FRN_KERNEL_XRES_N128 && kernel <= FRN_KERNEL_XRES_AUTO) {
-    if (K > 512)
-      return set_error(FRN_ERR_UNSUPPORTED, "the x-resident kernel takes K <= 512 (got %lld)",
-                       (long long)K);
-    static const int bns[4] = {128, 192, 224, 256};
-    const int bn = kernel == FRN_KERNEL_XRES_AUTO ? choose_xres_bn(M, N, K, sms / 2)
-                                                  : bns[kernel - FRN_KERNEL_XRES_N128];
-    return run_fused_linear_xres(p, bn, s);
-  }
-  if (kernel == FRN_KERNEL_PAIR_TS) {
-    if (K > 512)
-      return set_error(FRN_ERR_UNSUPPORTED, "the x-in-TMEM kernel takes K <= 512 (got %lld)",
-                       (long long)K);
-    return run_fused_linear_ts(p, s);
   }
   if (kernel == FRN_KERNEL_DECODE) {
     if (M > 128)

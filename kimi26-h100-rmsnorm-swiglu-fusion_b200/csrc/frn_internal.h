@@ -98,11 +98,6 @@ struct PairChoice {
 // (split outputs store whole 64-column chunks per part).
 PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs, bool tile64 = false);
 int run_fused_linear_pair(const LinearProblem& pr, PairChoice c, cudaStream_t s);
-// x-resident pair kernel for K <= 512 (frn_fused_linear_xres.cu).
-int choose_xres_bn(int64_t M, int64_t N, int64_t K, int pairs, bool tile64 = false);
-int run_fused_linear_xres(const LinearProblem& pr, int bn, cudaStream_t s);
-// x-in-TMEM pair kernel for K <= 512 (frn_fused_linear_ts.cu).
-int run_fused_linear_ts(const LinearProblem& pr, cudaStream_t s);
 // SwiGLU on the pair kernel: pr.w = [gate; up] with pr.N = 2 * inter rows;
 // the output has `inter` columns; tiles are 256 x bn output columns.
 int choose_swiglu_bn(int64_t M, int64_t inter, int64_t K, int pairs);

@@ -36,8 +36,6 @@ CU_SOURCES = [
     "frn_capi.cu",
     "frn_fused_linear.cu",
     "frn_fused_linear_pair.cu",
-    "frn_fused_linear_xres.cu",
-    "frn_fused_linear_ts.cu",
     "frn_decode.cu",
     "frn_fused_linear_w8.cu",
     "frn_normalize.cu",

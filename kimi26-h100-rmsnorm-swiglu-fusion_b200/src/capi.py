@@ -1,7 +1,7 @@
 """ctypes binding of the C ABI in include/frn_b200.h.
 
-This is the binding a non-torch host would write (see INTEGRATION.md for the
-cgo / JNI equivalents); the parity tests use it to call libfrn_b200.so
+This is the binding a non-torch host would write (a cgo or JNI host binds the
+same symbols the same way); the parity tests use it to call libfrn_b200.so
 exactly through its extern "C" entry points, passing raw device pointers,
 element strides and the current CUDA stream.
 """
@@ -40,12 +40,6 @@ FRN_KERNEL_WIDE_N128 = 11
 FRN_KERNEL_WIDE_N192 = 12
 FRN_KERNEL_WIDE_N224 = 13
 FRN_KERNEL_WIDE_N256 = 14
-FRN_KERNEL_XRES_N128 = 15
-FRN_KERNEL_XRES_N192 = 16
-FRN_KERNEL_XRES_N224 = 17
-FRN_KERNEL_XRES_N256 = 18
-FRN_KERNEL_XRES_AUTO = 19
-FRN_KERNEL_PAIR_TS = 20
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {
@@ -151,6 +145,14 @@ def _stream_ptr(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _on(device):
+    """Makes `device` current for the call: every frn_* entry point works on
+    the caller's current CUDA device (its SM count, its static scratch)."""
+    import torch
+
+    return torch.cuda.device(device)
+
+
 def workspace_size(dtype_code: int, M: int, N: int, K: int) -> int:
     return int(lib().frn_fused_rmsnorm_linear_workspace_size(dtype_code, M, N, K))
 
@@ -174,20 +176,22 @@ def fused_rmsnorm_linear(x, w, bias=None, eps: float = 1e-6, out=None,
         workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
     ws_ptr = workspace.data_ptr() if workspace is not None else None
     ws_bytes = workspace.numel() if workspace is not None else 0
-    rc = lib().frn_fused_rmsnorm_linear_ex(
-        dt, x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0),
-        bias.data_ptr() if bias is not None else None, float(eps), out.data_ptr(),
-        out.stride(0), ws_ptr, ws_bytes, int(kernel), _stream_ptr(x.device))
+    with _on(x.device):
+        rc = lib().frn_fused_rmsnorm_linear_ex(
+            dt, x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0),
+            bias.data_ptr() if bias is not None else None, float(eps), out.data_ptr(),
+            out.stride(0), ws_ptr, ws_bytes, int(kernel), _stream_ptr(x.device))
     check(rc, "frn_fused_rmsnorm_linear")
     return out
 
 
 def rmsnorm_normalize(x, raw_output, b_new, h: int, eps: float, threads: int = 256):
     """In-place raw_output = raw_output * inv_rms(x) + b_new through the C ABI."""
-    rc = lib().frn_rmsnorm_normalize(
-        _dtype_code(x), x.data_ptr(), x.stride(0), raw_output.data_ptr(), raw_output.stride(0),
-        b_new.data_ptr(), x.shape[0], h, raw_output.shape[1], float(eps), int(threads),
-        _stream_ptr(x.device))
+    with _on(x.device):
+        rc = lib().frn_rmsnorm_normalize(
+            _dtype_code(x), x.data_ptr(), x.stride(0), raw_output.data_ptr(), raw_output.stride(0),
+            b_new.data_ptr(), x.shape[0], h, raw_output.shape[1], float(eps), int(threads),
+            _stream_ptr(x.device))
     check(rc, "frn_rmsnorm_normalize")
     return raw_output
 
@@ -201,10 +205,11 @@ def fused_rmsnorm_linear_w8(x, wq, w_scale, bias=None, eps: float = 1e-6, out=No
     N = wq.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=x.dtype, device=x.device)
-    rc = lib().frn_fused_rmsnorm_linear_w8(
-        _dtype_code(x), x.data_ptr(), M, K, x.stride(0), wq.data_ptr(), N, wq.stride(0),
-        w_scale.data_ptr(), bias.data_ptr() if bias is not None else None, float(eps),
-        out.data_ptr(), out.stride(0), _stream_ptr(x.device))
+    with _on(x.device):
+        rc = lib().frn_fused_rmsnorm_linear_w8(
+            _dtype_code(x), x.data_ptr(), M, K, x.stride(0), wq.data_ptr(), N, wq.stride(0),
+            w_scale.data_ptr(), bias.data_ptr() if bias is not None else None, float(eps),
+            out.data_ptr(), out.stride(0), _stream_ptr(x.device))
     check(rc, "frn_fused_rmsnorm_linear_w8")
     return out
 
@@ -216,9 +221,10 @@ def quantize_int8_per_channel(w):
     N, K = w.shape
     q = torch.empty(N, K, dtype=torch.int8, device=w.device)
     scale = torch.empty(N, dtype=torch.float32, device=w.device)
-    rc = lib().frn_quantize_int8_per_channel(_dtype_code(w), w.data_ptr(), N, K, w.stride(0),
-                                             q.data_ptr(), K, scale.data_ptr(),
-                                             _stream_ptr(w.device))
+    with _on(w.device):
+        rc = lib().frn_quantize_int8_per_channel(_dtype_code(w), w.data_ptr(), N, K, w.stride(0),
+                                                 q.data_ptr(), K, scale.data_ptr(),
+                                                 _stream_ptr(w.device))
     check(rc, "frn_quantize_int8_per_channel")
     return q, scale
 
@@ -237,10 +243,11 @@ def fused_rmsnorm_linear_split(x, w, bias, eps: float, split_sizes, outs=None):
     cols = (c_int64 * n)(*[int(c) for c in split_sizes])
     ptrs = (c_void_p * n)(*[o.data_ptr() for o in outs])
     strides = (c_int64 * n)(*[o.stride(0) for o in outs])
-    rc = lib().frn_fused_rmsnorm_linear_split(
-        _dtype_code(x), x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0),
-        bias.data_ptr() if bias is not None else None, float(eps), n, cols, ptrs, strides,
-        _stream_ptr(x.device))
+    with _on(x.device):
+        rc = lib().frn_fused_rmsnorm_linear_split(
+            _dtype_code(x), x.data_ptr(), M, K, x.stride(0), w.data_ptr(), N, w.stride(0),
+            bias.data_ptr() if bias is not None else None, float(eps), n, cols, ptrs, strides,
+            _stream_ptr(x.device))
     check(rc, "frn_fused_rmsnorm_linear_split")
     return outs
 
@@ -249,10 +256,11 @@ def rmsnorm_swiglu(x, raw_output, output, b_new, h: int, intermediate: int, eps:
                    threads: int = 256):
     """output = silu(g * inv_rms + b_g) * (u * inv_rms + b_u) of a [gate | up]
     GEMM output, through the C ABI."""
-    rc = lib().frn_rmsnorm_swiglu(
-        _dtype_code(x), x.data_ptr(), x.stride(0), raw_output.data_ptr(), raw_output.stride(0),
-        output.data_ptr(), output.stride(0), b_new.data_ptr(), x.shape[0], h, intermediate,
-        float(eps), int(threads), _stream_ptr(x.device))
+    with _on(x.device):
+        rc = lib().frn_rmsnorm_swiglu(
+            _dtype_code(x), x.data_ptr(), x.stride(0), raw_output.data_ptr(), raw_output.stride(0),
+            output.data_ptr(), output.stride(0), b_new.data_ptr(), x.shape[0], h, intermediate,
+            float(eps), int(threads), _stream_ptr(x.device))
     check(rc, "frn_rmsnorm_swiglu")
     return output
 
@@ -270,10 +278,11 @@ def fused_rmsnorm_swiglu(x, w_combined, bias=None, eps: float = 1e-6, out=None):
     inter = w_combined.shape[0] // 2
     if out is None:
         out = torch.empty(M, inter, dtype=x.dtype, device=x.device)
-    rc = lib().frn_fused_rmsnorm_swiglu(
-        _dtype_code(x), x.data_ptr(), M, K, x.stride(0), w_combined.data_ptr(), inter,
-        w_combined.stride(0), bias.data_ptr() if bias is not None else None, float(eps),
-        out.data_ptr(), out.stride(0), _stream_ptr(x.device))
+    with _on(x.device):
+        rc = lib().frn_fused_rmsnorm_swiglu(
+            _dtype_code(x), x.data_ptr(), M, K, x.stride(0), w_combined.data_ptr(), inter,
+            w_combined.stride(0), bias.data_ptr() if bias is not None else None, float(eps),
+            out.data_ptr(), out.stride(0), _stream_ptr(x.device))
     check(rc, "frn_fused_rmsnorm_swiglu")
     return out
 
@@ -287,12 +296,15 @@ def gqa_decode_attention(q, k_cache, v_cache, scale: float, out=None, use_worksp
     T, Hkv = k_cache.shape[1], k_cache.shape[2]
     if out is None:
         out = torch.empty_like(q)
-    ws_bytes = int(lib().frn_gqa_decode_workspace_size(B, Hq, Hkv, D, T)) if use_workspace else 0
+    with _on(q.device):
+        ws_bytes = (int(lib().frn_gqa_decode_workspace_size(B, Hq, Hkv, D, T))
+                    if use_workspace else 0)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-    rc = lib().frn_gqa_decode_attention(
-        _dtype_code(q), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
-        B, Hq, Hkv, D, T, float(scale), ws.data_ptr() if ws is not None else None, ws_bytes,
-        _stream_ptr(q.device))
+    with _on(q.device):
+        rc = lib().frn_gqa_decode_attention(
+            _dtype_code(q), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+            B, Hq, Hkv, D, T, float(scale), ws.data_ptr() if ws is not None else None, ws_bytes,
+            _stream_ptr(q.device))
     check(rc, "frn_gqa_decode_attention")
     return out
 
@@ -302,9 +314,10 @@ def gqa_decode_attention_noalloc(q, k_cache, v_cache, scale: float, out):
     a workspace; `out` must be preallocated (nothing is allocated here)."""
     B, Hq, D = q.shape
     T, Hkv = k_cache.shape[1], k_cache.shape[2]
-    rc = lib().frn_gqa_decode_attention_noalloc(
-        _dtype_code(q), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
-        B, Hq, Hkv, D, T, float(scale), _stream_ptr(q.device))
+    with _on(q.device):
+        rc = lib().frn_gqa_decode_attention_noalloc(
+            _dtype_code(q), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(),
+            B, Hq, Hkv, D, T, float(scale), _stream_ptr(q.device))
     check(rc, "frn_gqa_decode_attention_noalloc")
     return out
 

@@ -6,9 +6,11 @@ Forward of every bf16/fp16 module is ONE launch of the sm_100a fused kernel
 (``denominator_cuda.fused_rmsnorm_linear``): the RMS reduction runs inside
 the GEMM and inv_rms / bias are applied to the fp32 accumulator.  V1 and V3
 named the reference's 256- vs 512-thread normalize kernels; both map to the
-same fused kernel here.  fp32 inputs, which the bf16/fp16 tensor-core kernel
-does not take, run as the reference does -- cuBLAS ``F.linear`` then the
-in-place ``rmsnorm_normalize(_512)`` kernel of this library.
+same fused kernel here.  The fused modules take bf16 and fp16 activations
+(the tcgen05 ``kind::f16`` tensor-core path); fp32 activations are refused
+with a RuntimeError rather than routed to a library GEMM.  The standalone
+``rmsnorm_normalize(_512)`` / ``rmsnorm_swiglu(_512)`` epilogue kernels still
+take fp32, fp16 and bf16 like the reference's.
 """
 
 from __future__ import annotations
@@ -16,7 +18,6 @@ from __future__ import annotations
 import os
 
 import torch
-import torch.nn.functional as F
 
 from src.load_cuda import denominator_cuda
 
@@ -41,37 +42,32 @@ def _nvtx_range(name: str):
 _TENSOR_CORE_DTYPES = (torch.bfloat16, torch.float16)
 
 
+def _require_tensor_core_dtype(x: torch.Tensor, what: str) -> None:
+    if x.dtype not in _TENSOR_CORE_DTYPES:
+        raise RuntimeError(
+            f"{what}: activations must be bfloat16 or float16 (got {x.dtype}); the fused "
+            "tcgen05 kernels have no fp32 path -- cast the module and its input to bf16")
+
+
 def _fused_2d(x_2d: torch.Tensor, W: torch.Tensor, b: torch.Tensor, h: int, eps: float,
               threads: int) -> torch.Tensor:
     """[M, K] -> [M, N] fused RMSNorm -> Linear on the current CUDA stream."""
     if x_2d.size(-1) != h:
         raise ValueError(f"x has {x_2d.size(-1)} features but the module was built for h={h}")
-    if x_2d.dtype in _TENSOR_CORE_DTYPES:
-        return denominator_cuda.fused_rmsnorm_linear(x_2d, W, b, float(eps))
-    raw = F.linear(x_2d, W)
-    normalize = (denominator_cuda.rmsnorm_normalize_512 if threads == 512
-                 else denominator_cuda.rmsnorm_normalize)
-    normalize(x_2d, raw, b, h, float(eps))
-    return raw
+    _require_tensor_core_dtype(x_2d, "fused RMSNorm+Linear")
+    return denominator_cuda.fused_rmsnorm_linear(x_2d, W, b, float(eps))
 
 
 def _swiglu_2d(x_2d: torch.Tensor, W: torch.Tensor, b: torch.Tensor, intermediate: int, h: int,
                eps: float, threads: int) -> torch.Tensor:
-    """[M, K] -> [M, I]: RMSNorm -> [gate | up] -> silu(gate) * up.  bf16/fp16 run
-    the single fused tcgen05 launch; fp32 runs F.linear and the reference's
-    rmsnorm_swiglu epilogue kernel (src/fused_forward.py:274-284 there)."""
+    """[M, K] -> [M, I]: RMSNorm -> [gate | up] -> silu(gate) * up in one fused
+    tcgen05 launch (bf16 / fp16)."""
     if x_2d.size(-1) != h:
         raise ValueError(f"x has {x_2d.size(-1)} features but the module was built for h={h}")
     if W.size(0) != 2 * intermediate:
         raise ValueError(f"W_combined has {W.size(0)} rows, expected 2*{intermediate}")
-    if x_2d.dtype in _TENSOR_CORE_DTYPES:
-        return denominator_cuda.fused_rmsnorm_swiglu(x_2d, W, b, float(eps))
-    raw = F.linear(x_2d, W)
-    out = torch.empty(x_2d.size(0), intermediate, dtype=x_2d.dtype, device=x_2d.device)
-    swiglu = (denominator_cuda.rmsnorm_swiglu_512 if threads == 512
-              else denominator_cuda.rmsnorm_swiglu)
-    swiglu(x_2d.contiguous(), raw, out, b, h, intermediate, float(eps))
-    return out
+    _require_tensor_core_dtype(x_2d, "fused RMSNorm+SwiGLU")
+    return denominator_cuda.fused_rmsnorm_swiglu(x_2d, W, b, float(eps))
 
 
 def _apply(x: torch.Tensor, W: torch.Tensor, b: torch.Tensor, h: int, eps: float,
@@ -135,7 +131,8 @@ class _FusedRMSNormCombinedBase(torch.nn.Module):
             if x_2d.size(-1) != self.h:
                 raise ValueError(f"x has {x_2d.size(-1)} features but the module was built "
                                  f"for h={self.h}")
-            if x_2d.dtype in _TENSOR_CORE_DTYPES and self._split_ok(x_2d.size(0)):
+            _require_tensor_core_dtype(x_2d, "fused RMSNorm+Linear (combined)")
+            if self._split_ok(x_2d.size(0)):
                 # One launch writes every part straight into its own tensor.
                 parts = denominator_cuda.fused_rmsnorm_linear_split(
                     x_2d, self.W_combined, self.b_combined, float(self.eps),

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference package (``src``) with ``src.load_cuda`` replaced by
 a stub -- its CUDA kernels are not needed for any of the functions used here
@@ -92,7 +92,8 @@ def tiny_deepseek_v3(seed: int = 7):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the reference checkout (read only)")
     args = ap.parse_args()
     bk, bq, pk, wt = _load_reference(args.reference)
 

@@ -95,3 +95,19 @@ def test_build_stamp_is_relocatable_and_covers_every_header():
     assert headers <= set(_build.HEADERS), headers - set(_build.HEADERS)
     sources = {f for f in os.listdir(csrc) if f.endswith(".cu")}
     assert sources == set(_build.CU_SOURCES)
+
+
+def test_gqa_workspace_fits_the_static_scratch_on_b200():
+    """With G <= 8 and head_dim <= 128 the split rule (about three CTAs per SM
+    over batch x KV heads) keeps the fp32 split path's workspace under the
+    2 MiB static scratch of frn_gqa_decode_attention_noalloc on a 148-SM part,
+    so that entry point rejects no valid shape there.  Host-only query."""
+    f = capi.lib().frn_gqa_decode_workspace_size
+    worst = 0
+    for B in (1, 2, 3, 4, 7, 16, 64, 300):
+        for Hkv in (1, 2, 4, 8, 32):
+            for G in (1, 2, 4, 8):
+                for D in (64, 128):
+                    for T in (1, 33, 1000, 8192, 131072):
+                        worst = max(worst, f(B, Hkv * G, Hkv, D, T))
+    assert 0 < worst <= 3 * 148 * 8 * (128 + 2) * 4 <= 2 << 20

@@ -57,68 +57,6 @@ ALL_KERNELS = [capi.FRN_KERNEL_TILE_N128, capi.FRN_KERNEL_TILE_N192, capi.FRN_KE
                capi.FRN_KERNEL_WIDE_N192, capi.FRN_KERNEL_WIDE_N224, capi.FRN_KERNEL_WIDE_N256]
 
 
-XRES_KERNELS = [capi.FRN_KERNEL_XRES_N128, capi.FRN_KERNEL_XRES_N192, capi.FRN_KERNEL_XRES_N224,
-                capi.FRN_KERNEL_XRES_N256, capi.FRN_KERNEL_XRES_AUTO]
-
-
-@pytest.mark.parametrize("kernel", XRES_KERNELS)
-@pytest.mark.parametrize("shape", [(512, 512, 16384), (4096, 512, 16384), (1000, 512, 1000),
-                                   (129, 72, 264), (777, 320, 4104), (2000, 64, 520)])
-def test_x_resident_kernel(kernel, shape):
-    """K <= 512: x kept in shared memory across a pair's run of tiles."""
-    M, K, N = shape
-    x, gamma, W, W_new, b = _inputs(M, K, N, seed=M + N, bias=True)
-    out = capi.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), b.to(DEV), orc.EPS, kernel=kernel)
-    torch.cuda.synchronize()
-    _check(out, x, gamma, W, W_new, b, f"xres kernel{kernel} {shape}")
-    assert capi.device_error(0) == 0
-
-
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("shape", [(512, 512, 16384), (4096, 512, 16384), (1000, 512, 1000),
-                                   (129, 72, 264), (777, 320, 4104), (2000, 64, 520),
-                                   (25600, 64, 96), (256, 8, 8), (3, 448, 4160)])
-def test_x_in_tmem_kernel(dtype, shape):
-    """K <= 512: x moved into tensor memory once per run and used as the MMA's
-    A operand; tiles of 32..128 columns from per-pair unit ranges.  25600 rows
-    x 96 columns gives pairs several m-block runs each (x reloaded in TMEM)."""
-    M, K, N = shape
-    x, gamma, W, W_new, b = _inputs(M, K, N, seed=M + 3 * N, dtype=dtype, bias=True)
-    out = capi.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), b.to(DEV), orc.EPS,
-                                    kernel=capi.FRN_KERNEL_PAIR_TS)
-    torch.cuda.synchronize()
-    _check(out, x, gamma, W, W_new, b, f"ts {dtype} {shape}")
-    assert capi.device_error(0) == 0
-
-
-def test_x_in_tmem_kernel_deterministic_and_strided():
-    M, K, N = 512, 512, 16384
-    x, gamma, W, W_new, b = _inputs(M, K, N, seed=77)
-    full = torch.zeros(M, 576, dtype=torch.bfloat16)
-    full[:, :K] = x
-    full[:, K:] = 7.0  # must not enter the RMS
-    xd = full.to(DEV)[:, :K]
-    outs = [capi.fused_rmsnorm_linear(xd, W_new.to(DEV), None, orc.EPS,
-                                      kernel=capi.FRN_KERNEL_PAIR_TS) for _ in range(3)]
-    torch.cuda.synchronize()
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
-    _check(outs[0], x, gamma, W, W_new, b, "ts strided")
-
-
-def test_x_in_tmem_rejects_long_k():
-    x, gamma, W, W_new, b = _inputs(256, 576, 64, seed=1)
-    with pytest.raises(capi.FrnError, match="K <= 512"):
-        capi.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), None, orc.EPS,
-                                  kernel=capi.FRN_KERNEL_PAIR_TS)
-
-
-def test_x_resident_rejects_long_k():
-    x, gamma, W, W_new, b = _inputs(256, 576, 64, seed=1)
-    with pytest.raises(capi.FrnError, match="K <= 512"):
-        capi.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), None, orc.EPS,
-                                  kernel=capi.FRN_KERNEL_XRES_AUTO)
-
-
 @pytest.mark.parametrize("kernel", ALL_KERNELS)
 @pytest.mark.parametrize("shape", [(512, 1536, 12288), (512, 512, 16384), (300, 1536, 1000),
                                    (129, 72, 264)])

@@ -75,14 +75,23 @@ def test_combined_module_splits():
     torch.testing.assert_close(torch.cat([q, k, v], -1).float().cpu(), ref, atol=2e-2, rtol=2e-2)
 
 
-def test_fp32_module_runs_library_gemm_plus_normalize():
+def test_fp32_activations_are_refused_not_rerouted():
+    """The fused modules have no fp32 kernel and do not fall back to a library
+    GEMM: fp32 input raises a RuntimeError that names the fix."""
     M, K, N = 64, 256, 384
     x, gamma, W = orc.make_inputs(M, K, N, seed=24, dtype=torch.float32)
     W_new = orc.fold_gamma(W, gamma)
     b = torch.zeros(N)
-    m = fused_forward.FusedRMSNormLinearV1(W_new.to(DEV), b.to(DEV), K, orc.EPS)
-    out = m(x.to(DEV)).cpu()
-    torch.testing.assert_close(out, orc.fp32_truth(x, W_new, b, orc.EPS), atol=1e-3, rtol=1e-3)
+    for cls in (fused_forward.FusedRMSNormLinearV1, fused_forward.FusedRMSNormLinearV3):
+        m = cls(W_new.to(DEV), b.to(DEV), K, orc.EPS)
+        with pytest.raises(RuntimeError, match="bfloat16 or float16"):
+            m(x.to(DEV))
+    comb = fused_forward.FusedRMSNormCombinedLinearV1(W_new.to(DEV), b.to(DEV), [256, 128], K,
+                                                      orc.EPS)
+    with pytest.raises(RuntimeError, match="bfloat16 or float16"):
+        comb(x.to(DEV))
+    with pytest.raises(RuntimeError, match="bf16 and fp16"):
+        denominator_cuda.fused_rmsnorm_linear(x.to(DEV), W_new.to(DEV), b.to(DEV), orc.EPS)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])

@@ -88,3 +88,16 @@ def test_patch_llama_structure_on_cpu():
             assert "forward" in vars(layer) and "forward" in vars(layer.self_attn)
     with _pytest.raises(ValueError, match="Unknown variant"):
         patch_llama_model(LlamaForCausalLM(cfg), device="cpu", variant="V2")
+
+
+def test_fp32_activations_refused_before_any_launch():
+    """fp32 has no tensor-core path here and no library-GEMM fallback: the
+    modules raise before touching the device."""
+    W = torch.randn(16, 8)
+    b = torch.zeros(16)
+    for cls in (fused_forward.FusedRMSNormLinearV1, fused_forward.FusedRMSNormLinearV3):
+        with pytest.raises(RuntimeError, match="bfloat16 or float16"):
+            cls(W, b, 8, 1e-5)(torch.randn(2, 8))
+    sw = fused_forward.FusedRMSNormSwiGLUV1(torch.randn(16, 8), torch.zeros(16), 8, 8, 1e-5)
+    with pytest.raises(RuntimeError, match="bfloat16 or float16"):
+        sw(torch.randn(2, 8))
