@@ -9,11 +9,19 @@ Steps rotate over enough (x, W, out) buffer sets that the working set is
 about twice the 126 MB L2, so every call streams W and out from/to HBM.  The
 K timed steps are replayed from CUDA graphs (one node per call), bracketed by a
 barrier and torch.cuda.synchronize() on both sides, timed with CUDA events on
-the launching stream; the max over ranks is reported.  With N > 1 (torchrun,
-one rank per GPU) each rank processes its own 512-token shard with its own
-weight replica and there is no collective on the data path (weak scaling).
+the launching stream.  That K-step window is repeated (at least 5 times and
+until about 200 ms have been timed); each window's time is the max over ranks
+and the reported time is the median window.  With N > 1 (torchrun, one rank
+per GPU) each rank processes its own 512-token shard with its own weight
+replica and there is no collective on the data path (weak scaling).
 
-One JSON line is printed by rank 0; see DESIGN.md for every key.
+Besides the headline, the JSON line carries the token-partitioned
+configurations at this N: ``long_prefill`` (q_b and kv_b at 4096 tokens in
+total, 4096/N rows per rank, strong scaling) and ``int8_stack`` (61 layers of
+int8 q_b + int8 kv_b at 2048 tokens in total, 2048/N rows per rank).
+
+One JSON line is printed by rank 0.  ``--profile CASE`` instead runs one case's
+kernel a few times with no timing, for ncu captures.
 """
 from __future__ import annotations
 
@@ -55,18 +63,36 @@ NVML_REASONS = {
 }
 
 
+# Cases --profile can run (one kernel, a few launches, no timing): the linear
+# shapes above plus the int8, SwiGLU and GQA workloads of the sweep.
+PROFILE_CASES = sorted(list(SHAPES) + ["int8_q_b", "int8_q_b_256", "int8_kv_b_256",
+                                       "swiglu_prefill", "swiglu_decode_m8",
+                                       "gqa_decode_llama"])
+# Token-partitioned configurations: (total tokens, hidden, out).
+LONG_PREFILL = {"kimi_q_b_long": (4096, 1536, 12288), "kimi_kv_b_long": (4096, 512, 16384)}
+STACK_LAYERS = 61
+STACK_TOKENS = 2048
+STACK_SHAPES = (("q_b", 1536, 12288), ("kv_b", 512, 16384))
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(SHAPES), default=HEADLINE)
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-config sweep")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-partitioned", action="store_true",
+                    help="skip the long_prefill and int8_stack configurations")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--min-timed-ms", type=float, default=200.0,
+                    help="repeat the K-step window until this much has been timed")
+    ap.add_argument("--profile", choices=PROFILE_CASES,
+                    help="run CASE's kernel --steps times after --warmup calls, untimed (ncu)")
     ap.add_argument("--gqa-only", action="store_true",
-                    help="time only the GQA decode-attention workload (one JSON line; for profiling)")
+                    help="time only the GQA decode-attention workload (one JSON line)")
     return ap.parse_args()
 
 
@@ -76,6 +102,11 @@ def flops_of(M, K, N):
 
 def bytes_of(M, K, N, elem=2):
     return float(elem) * (M * K + N * K + M * N)
+
+
+def bytes_of_w8(M, K, N):
+    """x and out in bf16, int8 weight, fp32 per-channel scales."""
+    return 2.0 * M * K + N * K + 4.0 * N + 2.0 * M * N
 
 
 def read_peaks():
@@ -88,6 +119,10 @@ def read_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def roofline_us(flops, nbytes, hbm_gbs, tflops_peak):
+    return max(flops / (tflops_peak * 1e12), nbytes / (hbm_gbs * 1e9)) * 1e6
+
+
 def read_profiled_traffic(kernel: str, workload: str):
     """Per-launch DRAM bytes recorded from an ncu capture in profiles/."""
     path = os.path.join(REPO, "profiles", f"{kernel}__{workload}.md")
@@ -97,6 +132,59 @@ def read_profiled_traffic(kernel: str, workload: str):
         return None
     m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", text)
     return float(m.group(1)) if m else None
+
+
+def make_config(name, world):
+    """The workload identity, the same dict in both arms."""
+    M, K, N = SHAPES[name]
+    return {"workload": name, "tokens_per_gpu": M, "hidden": K, "out": N,
+            "parallelism": (f"dp{world}: token-partitioned, replicated W, no collective"
+                            if world > 1 else "single GPU"),
+            "l2": "GPU arm: each call's (x, W, out) set rotates among sets totalling about "
+                  "twice the 126 MB L2 (flushed by rotation); CPU reference arm: host memory"}
+
+
+class Comm:
+    """Barrier / max / gather over the ranks of one job (no-ops at one rank)."""
+
+    def __init__(self, world, local_rank, device):
+        self.world, self.local_rank, self.device = world, local_rank, device
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[self.local_rank])
+
+    def max_(self, values):
+        import torch
+
+        t = torch.tensor(values, device=self.device, dtype=torch.float64)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def gather(self, value):
+        import torch
+
+        t = torch.tensor([value], device=self.device, dtype=torch.float64)
+        if self.world == 1:
+            return [value]
+        import torch.distributed as dist
+
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+
+LOCAL = None  # Comm of a single rank, set in run_ours
+
+
+def spread(values):
+    return {"min": round(min(values), 3), "median": round(statistics.median(values), 3),
+            "max": round(max(values), 3)}
 
 
 # ----------------------------------------------------------------- clocks
@@ -194,7 +282,7 @@ def unfused_torch(x, gamma, W, eps):
 class Rotation:
     """S independent (x, W_fused, out) sets; S chosen so S * set_bytes >= 2 * L2."""
 
-    def __init__(self, M, K, N, device, seed=1234, min_sets=2):
+    def __init__(self, M, K, N, device, seed=1234, min_sets=2, w_seed=None):
         import torch
 
         set_bytes = bytes_of(M, K, N)
@@ -202,6 +290,8 @@ class Rotation:
         self.xs, self.gammas, self.ws, self.wf, self.outs = [], [], [], [], []
         for s in range(self.S):
             x, gamma, W = gpu_inputs(M, K, N, seed + s, device)
+            if w_seed is not None:  # weights shared by every rank (replicas)
+                _, gamma, W = gpu_inputs(1, K, N, w_seed + s, device)
             self.xs.append(x)
             self.gammas.append(gamma)
             self.ws.append(W)
@@ -214,9 +304,12 @@ class Rotation:
         return f"rotating {self.S} (x, W, out) sets, {tot / 1e6:.0f} MB > 126 MB L2"
 
 
-def time_steps(fns, steps, warmup, barrier=None):
-    """Run `steps` calls fns[i % S], replayed from CUDA graphs; returns the
-    elapsed ms of exactly `steps` calls (events on the launching stream)."""
+def time_windows(fns, steps, warmup, comm, min_total_ms=200.0, max_windows=2000):
+    """Times `steps` calls fns[i % S], replayed from CUDA graphs, as one window
+    bracketed by a barrier and a synchronize on both sides (CUDA events on the
+    launching stream).  The window is repeated (>= 5 times, until about
+    `min_total_ms` has been timed; every rank runs the same count).  Returns
+    (this rank's ms per window, max over ranks per window)."""
     import torch
 
     S = len(fns)
@@ -241,24 +334,36 @@ def time_steps(fns, steps, warmup, barrier=None):
     for _ in range(max(1, math.ceil(warmup / S))):
         full.replay()
     torch.cuda.synchronize()
-    if barrier:
-        barrier()
-    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps // S):
-        full.replay()
-    if part is not None:
-        part.replay()
-    end.record()
-    end.synchronize()
-    torch.cuda.synchronize()
-    if barrier:
-        barrier()
-    ms = start.elapsed_time(end)
+
+    def window():
+        comm.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(steps // S):
+            full.replay()
+        if part is not None:
+            part.replay()
+        end.record()
+        end.synchronize()
+        torch.cuda.synchronize()
+        comm.barrier()
+        return start.elapsed_time(end)
+
+    first = comm.max_([window()])[0]
+    n = int(min(max_windows, max(5, math.ceil(min_total_ms / max(first, 1e-3)))))
+    local = [window() for _ in range(n)]
+    job = comm.max_(local)
     del full, part
-    return ms
+    return local, job
+
+
+def time_steps(fns, steps, warmup, min_total_ms=50.0):
+    """ms of `steps` calls on this GPU alone: the median of windows as in
+    time_windows (the sweep rows)."""
+    local, _ = time_windows(fns, steps, warmup, Comm(1, 0, "cpu"), min_total_ms)
+    return statistics.median(local)
 
 
 # ------------------------------------------------------------ CPU baseline
@@ -289,7 +394,9 @@ def cpu_reference_timing(M, K, N, seconds, threads=None):
 
 def run_reference(args):
     """--impl reference: the reference's own CPU implementation of the path
-    (oracle port of linear(SimpleRMSNorm(x)), bf16, all host threads)."""
+    (oracle port of linear(SimpleRMSNorm(x)), bf16, all host threads).  A step
+    is one full call on the workload; the K-step window is repeated until about
+    two seconds have been timed and the median window is reported."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -302,22 +409,32 @@ def run_reference(args):
     x, gamma, W = orc.make_inputs(M, K, N, seed=1234)
     for _ in range(args.warmup):
         orc.unfused_reference(x, gamma, W, None, EPS)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        orc.unfused_reference(x, gamma, W, None, EPS)
-    el = time.perf_counter() - t0
+    windows, total = [], 0.0
+    while len(windows) < 5 or (total < 2.0 and len(windows) < 1000):
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            orc.unfused_reference(x, gamma, W, None, EPS)
+        el = time.perf_counter() - t0
+        windows.append(el)
+        total += el
+    el = statistics.median(windows)
     value = flops_of(M, K, N) * args.steps / el / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: x~N(0,1), gamma~1+0.1N(0,1), W~N(0,1/K), seed 1234",
-        "config": {"workload": args.config, "tokens": M, "hidden": K, "out": N,
-                   "path": "reference CPU torch path linear(SimpleRMSNorm(x)) (oracle port)"},
+        "data": "synthetic: x~N(0,1), gamma~1+0.1N(0,1), W~N(0,1/K) (gamma folded), "
+                "seeded; no checkpoint",
+        "config": make_config(args.config, args.gpus),
+        "timing": {"windows": len(windows), "window_ms": spread([w * 1e3 for w in windows]),
+                   "method": "perf_counter around K full calls per window, median window",
+                   "path": "reference CPU torch path linear(SimpleRMSNorm(x)) (oracle port), "
+                           "rank 0 only"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                          "kind": "port",
-                         "sample": f"{args.steps} full calls at {M}x{K}->{N}"},
+                         "sample": f"{len(windows)} windows of {args.steps} full calls at "
+                                   f"{M}x{K}->{N}, {total:.1f} s in all"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -341,9 +458,9 @@ def run_ours(args):
 
         dist.init_process_group("nccl", device_id=device,
                                 timeout=datetime.timedelta(seconds=300))
-        barrier = lambda: dist.barrier(device_ids=[local_rank])  # noqa: E731
-    else:
-        barrier = None
+    comm = Comm(world, local_rank, device)
+    global LOCAL
+    LOCAL = Comm(1, local_rank, device)
 
     from src.load_cuda import denominator_cuda
 
@@ -355,21 +472,91 @@ def run_ours(args):
         for i in range(rot.S)
     ]
     with ClockSampler(local_rank) as clocks:
-        ms = time_steps(fns, args.steps, args.warmup, barrier)
-    t = torch.tensor([ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+        local, job = time_windows(fns, args.steps, args.warmup, comm, args.min_timed_ms)
+    ms = statistics.median(job)
     flops = flops_of(M, K, N)
     value = world * flops * args.steps / (ms / 1e3) / 1e12
     per_launch_s = ms / 1e3 / args.steps
+    rank_us = comm.gather(statistics.median(local) * 1e3 / args.steps)
 
-    # ---- e2e through the public API with pinned host buffers.  Every step
-    # copies its x in from pinned host memory, runs the op and copies its whole
-    # output back; steps are pipelined the way a server overlaps requests:
-    # copy-in, compute and copy-out on three streams, two buffer sets, so step
-    # i's device-to-host read overlaps step i+1's copy-in and kernel.
-    e2e_steps = max(1, min(args.steps, 200))
+    e2e = run_e2e(args, denominator_cuda, rot, comm, device, M, K, N, world)
+
+    hbm_gbs, tflops_peak, peak_src = read_peaks()
+    roof_time = max(flops / (tflops_peak * 1e12), bytes_of(M, K, N) / (hbm_gbs * 1e9))
+    bound = "tensor" if flops / (tflops_peak * 1e12) >= bytes_of(M, K, N) / (hbm_gbs * 1e9) \
+        else "hbm"
+    if bound == "tensor":
+        achieved, peak, unit = flops / per_launch_s / 1e12, tflops_peak, "TFLOP/s"
+    else:
+        achieved, peak, unit = bytes_of(M, K, N) / per_launch_s / 1e9, hbm_gbs, "GB/s"
+    roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                "frac": achieved / peak, "traffic": read_profiled_traffic(
+                    "fused_rmsnorm_linear" if M > 128 else "fused_rmsnorm_linear_decode",
+                    args.config),
+                "peak_source": f"{peak_src} (MEASURED_PEAKS.json burst figures)"
+                if peak_src == "measured" else "fallback",
+                "roofline_frac_of_max_time": roof_time / per_launch_s,
+                "kernel": ("fused_rmsnorm_linear_pair_kernel" if M > 128
+                           else "fused_rmsnorm_linear_decode_kernel"),
+                "algorithmic_bytes_per_launch": bytes_of(M, K, N),
+                "algorithmic_flops_per_launch": flops}
+
+    partitioned = {}
+    if not args.no_partitioned:
+        partitioned["long_prefill"] = run_long_prefill(args, denominator_cuda, comm, device,
+                                                       rank, world, hbm_gbs, tflops_peak)
+        partitioned["int8_stack"] = run_int8_stack(args, denominator_cuda, comm, device, rank,
+                                                   world, hbm_gbs, tflops_peak)
+
+    sweep = None
+    if rank == 0 and world == 1 and not args.no_sweep:
+        sweep = run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_timing(M, K, N, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: x~N(0,1), gamma~1+0.1N(0,1), W~N(0,1/K) (gamma folded), "
+                    "seeded; no checkpoint",
+            "config": make_config(args.config, world),
+            "timing": {"windows": len(job), "us_per_call": ms * 1e3 / args.steps,
+                       "window_ms_max_over_ranks": spread(job),
+                       "us_per_call_by_rank": spread(rank_us),
+                       "method": "CUDA graph replay of K calls per window, CUDA events on "
+                                 "the launching stream, barrier + synchronize around each "
+                                 "window; median over windows of the max over ranks",
+                       "l2": rot.describe()},
+            "e2e": e2e,
+            "gpu_launches": args.steps * len(job),
+            "gpu_launches_detail": "fused_rmsnorm_linear_pair_kernel, K per window x windows "
+                                   "of the headline timed region (one per step)",
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+        }
+        line.update(partitioned)
+        if sweep is not None:
+            line["sweep"] = sweep
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def run_e2e(args, denominator_cuda, rot, comm, device, M, K, N, world):
+    """The headline metric end to end through the public API with pinned host
+    buffers: every step copies its x in from pinned host memory, runs the op
+    and copies its whole output back.  Steps are pipelined the way a server
+    overlaps requests: copy-in, compute and copy-out on three streams, two
+    buffer sets, so step i's device-to-host read overlaps step i+1's copy-in
+    and kernel.  Windows of K steps, median of the max over ranks."""
+    import torch
+
+    flops = flops_of(M, K, N)
     x_host = rot.xs[0].cpu().pin_memory()
     out_host = [torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     xd = [torch.empty_like(rot.xs[0]) for _ in range(2)]
@@ -396,84 +583,142 @@ def run_ours(args):
             ev_out[j].record(s_out)
 
     cur = torch.cuda.current_stream(device)
-    for i in range(4):
+    for i in range(max(4, args.warmup)):
         e2e_step(i)
     torch.cuda.synchronize()
-    if barrier:
-        barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(cur)
-    for st in (s_in, s_cmp, s_out):
-        st.wait_event(e0)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    for st in (s_in, s_cmp, s_out):
-        cur.wait_stream(st)
-    e1.record(cur)
-    e1.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * flops * e2e_steps / (float(te.item()) / 1e3) / 1e12
 
-    hbm_gbs, tflops_peak, peak_src = read_peaks()
-    roof_time = max(flops / (tflops_peak * 1e12), bytes_of(M, K, N) / (hbm_gbs * 1e9))
-    bound = "tensor" if flops / (tflops_peak * 1e12) >= bytes_of(M, K, N) / (hbm_gbs * 1e9) \
-        else "hbm"
-    if bound == "tensor":
-        achieved, peak, unit = flops / per_launch_s / 1e12, tflops_peak, "TFLOP/s"
-    else:
-        achieved, peak, unit = bytes_of(M, K, N) / per_launch_s / 1e9, hbm_gbs, "GB/s"
-    roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                "frac": achieved / peak, "traffic": read_profiled_traffic(
-                    "fused_rmsnorm_linear" if M > 128 else "fused_rmsnorm_linear_decode",
-                    args.config),
-                "peak_source": f"{peak_src} (MEASURED_PEAKS.json burst figures)"
-                if peak_src == "measured" else "fallback",
-                "roofline_frac_of_max_time": roof_time / per_launch_s,
-                "kernel": ("fused_rmsnorm_linear_pair_kernel" if M > 128
-                           else "fused_rmsnorm_linear_decode_kernel"),
-                "algorithmic_bytes_per_launch": bytes_of(M, K, N),
-                "algorithmic_flops_per_launch": flops}
+    def window():
+        comm.barrier()
+        torch.cuda.synchronize()
+        e0.record(cur)
+        for st in (s_in, s_cmp, s_out):
+            st.wait_event(e0)
+        for i in range(args.steps):
+            e2e_step(i)
+        for st in (s_in, s_cmp, s_out):
+            cur.wait_stream(st)
+        e1.record(cur)
+        e1.synchronize()
+        comm.barrier()
+        return e0.elapsed_time(e1)
 
-    sweep = None
-    if rank == 0 and world == 1 and not args.no_sweep:
-        sweep = run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_reference_timing(M, K, N, args.cpu_seconds)
+    first = comm.max_([window()])[0]
+    n = int(min(500, max(5, math.ceil(args.min_timed_ms / max(first, 1e-3)))))
+    local = [window() for _ in range(n)]
+    job = comm.max_(local)
+    ms = statistics.median(job)
+    step_us_by_rank = comm.gather(statistics.median(local) * 1e3 / args.steps)
+    d2h = M * N * 2
+    return {"value": world * flops * args.steps / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": d2h,
+            "steps": args.steps, "windows": n,
+            "us_per_step_by_rank": spread(step_us_by_rank),
+            "d2h_gbs_per_rank": spread([d2h / us / 1e3 for us in step_us_by_rank]),
+            "path": "denominator_cuda.fused_rmsnorm_linear, pinned host x -> HBM, out -> "
+                    "pinned host, W resident; copy-in / kernel / copy-out on three streams, "
+                    "two buffer sets (step i's read-back overlaps step i+1)"}
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: x~N(0,1), gamma~1+0.1N(0,1), W~N(0,1/K) (gamma folded), "
-                    "seeded; no checkpoint",
-            "config": {"workload": args.config, "tokens_per_gpu": M, "hidden": K, "out": N,
-                       "parallelism": f"token-partitioned x{world}, replicated W, "
-                                      "no collective" if world > 1 else "single GPU",
-                       "l2": rot.describe(), "timing": "CUDA graph replay of K calls, "
-                                                       "CUDA events on the launching stream",
-                       "us_per_call": ms * 1e3 / args.steps},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
-                    "steps": e2e_steps,
-                    "path": "denominator_cuda.fused_rmsnorm_linear, pinned host x -> HBM, "
-                            "out -> pinned host, W resident; copy-in / kernel / copy-out "
-                            "on three streams, two buffer sets (step i's read-back "
-                            "overlaps step i+1)"},
-            "gpu_launches": args.steps,
-            "roofline": roofline,
-            "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
+
+def run_long_prefill(args, denominator_cuda, comm, device, rank, world, hbm_gbs, tflops_peak):
+    """q_b and kv_b at 4096 tokens in total, token-partitioned: rank r takes its
+    contiguous share of the rows (4096 / N) against its own replica of W (the
+    same W on every rank), no collective.  Reports the job time (median window
+    of the max over ranks) against the per-GPU roofline of the busiest rank,
+    and, on rank 0, the whole 4096 rows on one GPU for the strong-scaling
+    ratio."""
+    import torch
+
+    from src.multigpu import shard_bounds
+
+    res = {}
+    steps = 20
+    for name, (M_tot, K, N) in LONG_PREFILL.items():
+        s, e = shard_bounds(M_tot, world, rank)
+        m = e - s
+        rot = Rotation(m, K, N, device, seed=4000 + 1000 * rank, w_seed=9000)
+        fns = [(lambda i=i: denominator_cuda.fused_rmsnorm_linear(rot.xs[i], rot.wf[i], None,
+                                                                  EPS, rot.outs[i]))
+               for i in range(rot.S)]
+        local, job = time_windows(fns, steps, 3, comm, 100.0)
+        job_us = statistics.median(job) * 1e3 / steps
+        rank_us = comm.gather(statistics.median(local) * 1e3 / steps)
+        m_max = max(shard_bounds(M_tot, world, r)[1] - shard_bounds(M_tot, world, r)[0]
+                    for r in range(world))
+        roof = roofline_us(flops_of(m_max, K, N), bytes_of(m_max, K, N), hbm_gbs, tflops_peak)
+        del rot, fns
+        torch.cuda.empty_cache()
+        one_gpu_us = None
+        if world > 1:
+            comm.barrier()
+            if rank == 0:  # the same total on one GPU, for the strong-scaling ratio
+                r1 = Rotation(M_tot, K, N, device, seed=4000, w_seed=9000)
+                f1 = [(lambda i=i: denominator_cuda.fused_rmsnorm_linear(
+                    r1.xs[i], r1.wf[i], None, EPS, r1.outs[i])) for i in range(r1.S)]
+                l1, _ = time_windows(f1, steps, 3, LOCAL, 100.0)
+                one_gpu_us = statistics.median(l1) * 1e3 / steps
+                del r1, f1
+                torch.cuda.empty_cache()
+            comm.barrier()
+        res[name] = {
+            "tokens_total": M_tot, "tokens_per_rank": m_max, "hidden": K, "out": N,
+            "job_us": round(job_us, 3), "us_by_rank": spread(rank_us),
+            "tflops_job": round(flops_of(M_tot, K, N) / job_us / 1e6, 1),
+            "roofline_us_per_gpu": round(roof, 3), "frac_of_roofline": round(roof / job_us, 3),
+            "one_gpu_us": round(one_gpu_us, 3) if one_gpu_us else None,
+            "strong_scaling_efficiency": (round(one_gpu_us / (world * job_us), 3)
+                                          if one_gpu_us else None),
         }
-        if sweep is not None:
-            line["sweep"] = sweep
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
+    return res
+
+
+def run_int8_stack(args, denominator_cuda, comm, device, rank, world, hbm_gbs, tflops_peak):
+    """61 Kimi layers of int8 q_b (1536 -> 12288) + int8 kv_b (512 -> 16384) at
+    2048 tokens in total, token-partitioned: rank r runs its share of the rows
+    through all 122 launches (weights quantized per output channel, replicated
+    and identical on every rank; every layer has its own x and output buffer,
+    several GB in all, so nothing stays in L2 from one stack to the next).  One
+    step = one whole stack, replayed from a CUDA graph."""
+    import torch
+
+    from src.multigpu import shard_bounds
+
+    s, e = shard_bounds(STACK_TOKENS, world, rank)
+    m = e - s
+    layers, xs, outs = [], [], []
+    for li in range(STACK_LAYERS):
+        for si, (_, K, N) in enumerate(STACK_SHAPES):
+            _, gamma, W = gpu_inputs(1, K, N, 20000 + 10 * li + si, device)
+            q, sc = denominator_cuda.quantize_int8_per_channel(W * gamma)
+            del W
+            layers.append(((q, sc), None))
+            g = torch.Generator(device=device).manual_seed(30000 + 1000 * rank + 10 * li + si)
+            xs.append(torch.randn(m, K, generator=g, device=device).to(torch.bfloat16))
+            outs.append(torch.empty(m, N, dtype=torch.bfloat16, device=device))
+    torch.cuda.synchronize()
+
+    def stack():
+        # The launches fused_stack_token_parallel makes, each writing into this
+        # rank's own preallocated output of its layer.
+        for x, ((q, sc), b), o in zip(xs, layers, outs):
+            denominator_cuda.fused_rmsnorm_linear_w8(x, q, sc, b, EPS, o)
+
+    local, job = time_windows([stack], 1, 2, comm, 100.0, max_windows=200)
+    job_us = statistics.median(job) * 1e3
+    rank_us = comm.gather(statistics.median(local) * 1e3)
+    m_max = max(shard_bounds(STACK_TOKENS, world, r)[1] - shard_bounds(STACK_TOKENS, world, r)[0]
+                for r in range(world))
+    roof = STACK_LAYERS * sum(roofline_us(flops_of(m_max, K, N), bytes_of_w8(m_max, K, N),
+                                          hbm_gbs, tflops_peak) for _, K, N in STACK_SHAPES)
+    fl = STACK_LAYERS * sum(flops_of(STACK_TOKENS, K, N) for _, K, N in STACK_SHAPES)
+    del layers, xs, outs
+    torch.cuda.empty_cache()
+    return {"layers": STACK_LAYERS, "tokens_total": STACK_TOKENS, "tokens_per_rank": m_max,
+            "launches_per_stack": 2 * STACK_LAYERS,
+            "job_us_per_stack": round(job_us, 3), "us_by_rank": spread(rank_us),
+            "us_per_layer_pair": round(job_us / STACK_LAYERS, 3),
+            "tflops_job": round(fl / job_us / 1e6, 1),
+            "roofline_us_per_stack": round(roof, 3), "frac_of_roofline": round(roof / job_us, 3)}
 
 
 def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
@@ -615,14 +860,59 @@ def sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps):
             "speedup_vs_reference_path": round(t_base / t_ours, 3)}
 
 
+def run_profile(args):
+    """--profile CASE: CASE's fused kernel launched --warmup + --steps times
+    eagerly on cuda:0 with no timing (for ncu: -k picks the kernel, -s skips
+    the warm-up launches).  Linear shapes rotate over sets larger than L2."""
+    import torch
+
+    from src.load_cuda import denominator_cuda
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    n = args.warmup + args.steps
+    case = args.profile
+    if case in SHAPES:
+        M, K, N = SHAPES[case]
+        rot = Rotation(M, K, N, device, seed=99)
+        for i in range(n):
+            j = i % rot.S
+            denominator_cuda.fused_rmsnorm_linear(rot.xs[j], rot.wf[j], None, EPS, rot.outs[j])
+    elif case.startswith("int8_"):
+        M, K, N = {"int8_q_b": (2048, 1536, 12288), "int8_q_b_256": (256, 1536, 12288),
+                   "int8_kv_b_256": (256, 512, 16384)}[case]
+        sets = []
+        for s in range(4):
+            x, gamma, W = gpu_inputs(M, K, N, 500 + s, device)
+            q, sc = denominator_cuda.quantize_int8_per_channel(W * gamma)
+            sets.append((x, q, sc, torch.empty(M, N, dtype=torch.bfloat16, device=device)))
+        for i in range(n):
+            x, q, sc, o = sets[i % 4]
+            denominator_cuda.fused_rmsnorm_linear_w8(x, q, sc, None, EPS, o)
+    elif case.startswith("swiglu_"):
+        M = 512 if case == "swiglu_prefill" else 8
+        K, inter = 4096, 14336
+        sets = []
+        for s in range(2):
+            x, gamma, W = gpu_inputs(M, K, 2 * inter, 700 + s, device)
+            sets.append((x, (W * gamma).contiguous(),
+                         torch.empty(M, inter, dtype=torch.bfloat16, device=device)))
+        for i in range(n):
+            x, Wc, o = sets[i % 2]
+            denominator_cuda.fused_rmsnorm_swiglu(x, Wc, None, EPS, o)
+    else:  # gqa_decode_llama
+        hbm_gbs, _, _ = read_peaks()
+        print(json.dumps({"gqa_decode_llama": sweep_gqa(denominator_cuda, device, hbm_gbs, n)}))
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": case, "launches": n}), flush=True)
+
+
 def main():
     args = parse_args()
     if args.gqa_only:
-        import torch
-        from src.load_cuda import denominator_cuda
-        hbm_gbs, _, _ = read_peaks()
-        print(json.dumps({"gqa_decode_llama": sweep_gqa(
-            denominator_cuda, torch.device("cuda"), hbm_gbs, 40)}))
+        args.profile = "gqa_decode_llama"
+    if args.profile:
+        run_profile(args)
         return
     if args.impl == "reference":
         run_reference(args)

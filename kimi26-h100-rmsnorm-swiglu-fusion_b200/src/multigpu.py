@@ -18,12 +18,17 @@ Two flavours of the token split:
   torch.distributed: every rank runs its own shard; ``gather=True`` adds an
   all-gather (for consumers that need every row on every rank).
 
+``fused_stack_token_parallel`` runs one rank's token shard through a whole
+stack of layers (the 61 q_b + kv_b pairs of Kimi K2.6, bf16 or int8 weights),
+again with no collective.
+
 ``ColumnParallelFusedLinear`` holds W[N-slice] per rank and all-gathers the
 [M, N/world] outputs into [M, N] over NCCL.
 
-The per-shard op is ``denominator_cuda.fused_rmsnorm_linear`` by default; it
-can be replaced (``op=``) so the partition / gather logic can be exercised on
-CPU ranks with the gloo backend.
+The per-shard op is ``denominator_cuda.fused_rmsnorm_linear`` (or
+``fused_rmsnorm_linear_w8`` for int8 weights, given as a ``(qweight,
+w_scale)`` pair) by default; it can be replaced (``op=``) so the partition /
+gather logic can be exercised on CPU ranks with the gloo backend.
 """
 
 from __future__ import annotations
@@ -39,6 +44,18 @@ def _default_op() -> FusedOp:
     from src.load_cuda import denominator_cuda
 
     return lambda x, w, b, eps: denominator_cuda.fused_rmsnorm_linear(x, w, b, float(eps))
+
+
+def _default_w8_op() -> FusedOp:
+    """The int8-weight fused op; `w` is a (qweight int8 [N, K], w_scale fp32 [N]) pair."""
+    from src.load_cuda import denominator_cuda
+
+    return lambda x, w, b, eps: denominator_cuda.fused_rmsnorm_linear_w8(x, w[0], w[1], b,
+                                                                         float(eps))
+
+
+def _out_features(w) -> int:
+    return (w[0] if isinstance(w, tuple) else w).shape[0]
 
 
 def shard_bounds(total: int, parts: int, index: int) -> tuple[int, int]:
@@ -63,22 +80,33 @@ def column_bounds(n: int, parts: int, index: int, align: int = 8) -> tuple[int, 
 class TokenPartitionedFusedLinear:
     """Fused RMSNorm -> Linear over several GPUs of one process, split by rows.
 
-    W_new / b_new are replicated to every device in `devices` at construction.
+    W_new / b_new are replicated to every device in `devices` at construction;
+    with ``int8=True`` W_new is quantized once per output channel (the
+    reference's absmax / 127 scheme) and the (qweight, w_scale) pair is what
+    gets replicated, so every device holds bit-identical int8 weights.
     ``__call__(x)`` returns a list of per-device outputs (rows in order) or,
     with ``out_device``, one [M, N] tensor gathered there.  Work on each device
     is enqueued on that device's current stream; the host does not wait.
     """
 
     def __init__(self, W_new: torch.Tensor, b_new: Optional[torch.Tensor], eps: float,
-                 devices: Sequence[torch.device | str | int], op: Optional[FusedOp] = None):
+                 devices: Sequence[torch.device | str | int], op: Optional[FusedOp] = None,
+                 int8: bool = False):
         self.devices = [torch.device(d) if not isinstance(d, int) else torch.device("cuda", d)
                         for d in devices]
         if not self.devices:
             raise ValueError("need at least one device")
         self.eps = float(eps)
-        self.weights = [W_new.to(d) for d in self.devices]
+        self.int8 = bool(int8)
+        if self.int8:
+            from src.quantized import quantize_int8_per_output_channel
+
+            q, scale = quantize_int8_per_output_channel(W_new)
+            self.weights = [(q.to(d), scale.to(d)) for d in self.devices]
+        else:
+            self.weights = [W_new.to(d) for d in self.devices]
         self.biases = [b_new.to(d) if b_new is not None else None for d in self.devices]
-        self.op = op or _default_op()
+        self.op = op or (_default_w8_op() if self.int8 else _default_op())
 
     def shards(self, m: int) -> list[tuple[int, int]]:
         return [shard_bounds(m, len(self.devices), i) for i in range(len(self.devices))]
@@ -93,11 +121,12 @@ class TokenPartitionedFusedLinear:
             if xs.device != dev:
                 xs = xs.to(dev, non_blocking=True)
             outs.append(self.op(xs, w, b, self.eps) if e > s else
-                        torch.empty(0, w.shape[0], dtype=x.dtype, device=dev))
+                        torch.empty(0, _out_features(w), dtype=x.dtype, device=dev))
         if out_device is None:
             return outs
         dst = torch.device(out_device)
-        full = torch.empty(x2.shape[0], self.weights[0].shape[0], dtype=x.dtype, device=dst)
+        full = torch.empty(x2.shape[0], _out_features(self.weights[0]), dtype=x.dtype,
+                           device=dst)
         for (s, e), o in zip(self.shards(x2.shape[0]), outs):
             if e > s:
                 full[s:e].copy_(o, non_blocking=True)
@@ -134,6 +163,27 @@ def fused_rmsnorm_linear_token_parallel(x_local: torch.Tensor, W_new: torch.Tens
     return torch.cat([b[:n] for b, n in zip(bufs, sizes)], dim=0)
 
 
+def fused_stack_token_parallel(xs_local: Sequence[torch.Tensor],
+                               layers: Sequence[tuple], eps: float, *,
+                               op: Optional[FusedOp] = None) -> list[torch.Tensor]:
+    """One rank's share of a token-partitioned stack of fused RMSNorm -> Linear
+    layers, e.g. the 61 (q_b, kv_b) pairs of Kimi K2.6 flattened to 122 layers.
+
+    ``layers[i]`` is ``(weight, bias)`` with ``weight`` either W_new [N, K]
+    (bf16 / fp16) or an int8 ``(qweight, w_scale)`` pair; ``xs_local[i]`` is
+    this rank's rows of layer i's input (every rank holds the same rows of
+    every layer: its token shard).  Every layer's weights are replicated on
+    every rank, so no collective runs; the launches go back to back on the
+    current stream.  Returns the per-layer outputs."""
+    if len(xs_local) != len(layers):
+        raise ValueError(f"{len(xs_local)} inputs for {len(layers)} layers")
+    outs = []
+    for x, (w, b) in zip(xs_local, layers):
+        f = op or (_default_w8_op() if isinstance(w, tuple) else _default_op())
+        outs.append(f(x, w, b, eps))
+    return outs
+
+
 class ColumnParallelFusedLinear:
     """Column (N) split: this rank holds W[cols] and produces out[:, cols].
 
@@ -165,10 +215,19 @@ class ColumnParallelFusedLinear:
         if not gather:
             return part.reshape(*lead, part.shape[-1])
         widths = [e - s for s, e in self.bounds]
-        mx = max(widths)
-        padded = part.new_zeros(x2.shape[0], mx)
-        padded[:, : part.shape[1]] = part
-        bufs = [torch.empty_like(padded) for _ in range(self.world)]
-        dist.all_gather(bufs, padded, group=self.group)
-        full = torch.cat([b[:, :w] for b, w in zip(bufs, widths)], dim=1)
+        m = x2.shape[0]
+        if len(set(widths)) == 1:
+            # Equal (e.g. head-aligned) slices: gather straight into one
+            # [world, M, w] buffer, then one layout copy to [M, world * w].
+            w = widths[0]
+            buf = part.new_empty(self.world * m, w)
+            dist.all_gather_into_tensor(buf, part.contiguous(), group=self.group)
+            full = buf.view(self.world, m, w).permute(1, 0, 2).reshape(m, self.n)
+        else:
+            mx = max(widths)
+            padded = part.new_zeros(m, mx)
+            padded[:, : part.shape[1]] = part
+            bufs = [torch.empty_like(padded) for _ in range(self.world)]
+            dist.all_gather(bufs, padded, group=self.group)
+            full = torch.cat([b[:, :w] for b, w in zip(bufs, widths)], dim=1)
         return full.reshape(*lead, self.n)

@@ -16,6 +16,12 @@ def _cpu_op(x, w, b, eps):
     return orc.fp32_truth(x, w, b, eps)
 
 
+def _cpu_w8_op(x, w, b, eps):
+    """The int8 kernel's math (inv_rms * scale * x.q^T + b) on the CPU."""
+    q, scale = w
+    return orc.int8_fp32_truth(x, q, scale, b, eps)
+
+
 def test_shard_bounds_cover_exactly():
     for total in (0, 1, 5, 512, 4097):
         for parts in (1, 2, 3, 8):
@@ -46,6 +52,33 @@ def test_single_process_token_partition_on_cpu_devices():
     torch.testing.assert_close(full.view(37, 24), _cpu_op(x, Wn, None, orc.EPS))
 
 
+def test_single_process_int8_partition_replicates_one_quantization():
+    x, gamma, W = orc.make_inputs(29, 64, 40, seed=2, dtype=torch.float32)
+    Wn = orc.fold_gamma(W, gamma)
+    tp = multigpu.TokenPartitionedFusedLinear(Wn, None, orc.EPS, ["cpu", "cpu"], op=_cpu_w8_op,
+                                              int8=True)
+    q, scale = orc.quantize_int8_per_output_channel(Wn)
+    for wq, ws in tp.weights:
+        assert torch.equal(wq, q) and torch.equal(ws, scale)
+    full = tp(x, out_device="cpu")
+    torch.testing.assert_close(full, _cpu_w8_op(x, (q, scale), None, orc.EPS))
+
+
+def test_stack_runs_each_layer_on_its_own_input():
+    layers, xs, want = [], [], []
+    for i, (K, N) in enumerate([(64, 48), (32, 80), (64, 48)]):
+        x, gamma, W = orc.make_inputs(10, K, N, seed=20 + i, dtype=torch.float32)
+        Wn = orc.fold_gamma(W, gamma)
+        layers.append((orc.quantize_int8_per_output_channel(Wn), None))
+        xs.append(x)
+        want.append(_cpu_w8_op(x, layers[-1][0], None, orc.EPS))
+    outs = multigpu.fused_stack_token_parallel(xs, layers, orc.EPS, op=_cpu_w8_op)
+    for o, w in zip(outs, want):
+        torch.testing.assert_close(o, w)
+    with pytest.raises(ValueError):
+        multigpu.fused_stack_token_parallel(xs[:2], layers, orc.EPS, op=_cpu_w8_op)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -73,10 +106,26 @@ def _worker(rank, world, port, results):
                                                  align=8, op=_cpu_op)
         colfull = col(x.view(5, 9, K))
         want = _cpu_op(x, Wn, b, orc.EPS)
+        # unequal column slices take the padded gather
+        col2 = multigpu.ColumnParallelFusedLinear(Wn, b, orc.EPS, rank=rank, world=world,
+                                                  align=16, op=_cpu_op)
+        assert len({e2 - s2 for s2, e2 in col2.bounds}) == 2
+        colfull2 = col2(x)
+        # a two-layer int8 stack, each rank on its own token shard of every layer
+        layers, xs, want_stack = [], [], []
+        for i, (Ki, Ni) in enumerate([(K, N), (2 * K, 24)]):
+            xi, gi, Wi = orc.make_inputs(M, Ki, Ni, seed=50 + i, dtype=torch.float32)
+            qs = orc.quantize_int8_per_output_channel(orc.fold_gamma(Wi, gi))
+            layers.append((qs, None))
+            xs.append(xi[s:e])
+            want_stack.append(_cpu_w8_op(xi, qs, None, orc.EPS)[s:e])
+        stack = multigpu.fused_stack_token_parallel(xs, layers, orc.EPS, op=_cpu_w8_op)
         results[rank] = (
             torch.allclose(local, want[s:e], atol=1e-5),
             torch.allclose(gathered, want, atol=1e-5),
-            torch.allclose(colfull.view(M, N), want, atol=1e-5),
+            torch.allclose(colfull.view(M, N), want, atol=1e-5)
+            and torch.allclose(colfull2, want, atol=1e-5),
+            all(torch.allclose(a, w) for a, w in zip(stack, want_stack)),
         )
     finally:
         dist.destroy_process_group()
@@ -94,7 +143,7 @@ def test_gloo_world2_token_and_column_parallel():
     for p in procs:
         p.join(90)
         assert p.exitcode == 0
-    assert dict(results) == {0: (True, True, True), 1: (True, True, True)}
+    assert dict(results) == {0: (True,) * 4, 1: (True,) * 4}
 
 
 # ------------------------------------------------ failure detection (host side)
