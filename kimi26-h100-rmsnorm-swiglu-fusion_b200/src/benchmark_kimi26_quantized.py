@@ -1,8 +1,15 @@
-"""Quantization-aware Kimi benchmark (same CLI and output lines as the
-reference's src/benchmark_kimi26_quantized.py:42-126), with the fused path
-running the int8-weight kernel instead of dequantize-then-F.linear.
+"""Quantization-aware Kimi benchmark with the reference's command line and
+key=value lines (reference src/benchmark_kimi26_quantized.py:42-126), the
+fused path running this library's int8-weight kernel instead of
+dequantize-then-F.linear:
 
     python -m src.benchmark_kimi26_quantized --config kimi_q_b --tokens 2048
+
+Inputs and timing come from the repository's bench.py (through
+src.benchmark_kimi26): the baseline is the reference's unfused quantized path
+(W quantized before gamma folding, norm then F.linear over the dequantized
+weight), its fused quantized path dequantizes W_fused and scales x by
+bf16(inv_rms); the int8 kernel is timed through FusedRMSNormLinearInt8.
 """
 
 from __future__ import annotations
@@ -10,12 +17,10 @@ from __future__ import annotations
 import argparse
 
 import torch
-import torch.nn as nn
 import torch.nn.functional as F
 
-from src.benchmark_kimi26 import CONFIGS, SimpleRMSNorm, bench
+from src.benchmark_kimi26 import CONFIGS, bench_module, shape_of, time_ms
 from src.quantized import FusedRMSNormLinearInt8, dequantize_int8, quantize_int8_per_output_channel
-from src.weight_transform import compute_fused_weights_rmsnorm
 
 
 def parse_args(argv=None) -> argparse.Namespace:
@@ -27,7 +32,6 @@ def parse_args(argv=None) -> argparse.Namespace:
     p.add_argument("--dtype", choices=["bfloat16", "float16"], default="bfloat16")
     p.add_argument("--warmup", type=int, default=30)
     p.add_argument("--iters", type=int, default=300)
-    p.add_argument("--cuda-events", action="store_true")
     return p.parse_args(argv)
 
 
@@ -35,36 +39,34 @@ def main(argv=None) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("CUDA is required.")
     args = parse_args(argv)
-    cfg = CONFIGS[args.config]
-    tokens = args.tokens or cfg["tokens"]
-    hidden = args.hidden or cfg["hidden"]
-    out = args.out or cfg["out"]
     dtype = getattr(torch, args.dtype)
-    device = torch.device("cuda")
+    tokens, hidden, out = shape_of(args)
+    b = bench_module()
+    x, gamma, W = (t.to(dtype) for t in b.gpu_inputs(tokens, hidden, out, 1234, "cuda"))
+    eps = b.EPS
+    q_w, q_scale = quantize_int8_per_output_channel(W)             # before folding
+    W_new = W * gamma
+    fused = FusedRMSNormLinearInt8(W_new, torch.zeros(out, dtype=dtype, device="cuda"),
+                                   hidden, eps)                      # after folding
 
-    torch.manual_seed(1234)
-    norm = SimpleRMSNorm(hidden, eps=1e-5).to(device=device, dtype=dtype)
-    linear = nn.Linear(hidden, out, bias=False).to(device=device, dtype=dtype)
-    x = torch.randn(tokens, hidden, device=device, dtype=dtype)
-    q_w, q_scale = quantize_int8_per_output_channel(linear.weight.detach())
+    def norm(t):
+        r = torch.rsqrt(t.float().pow(2).mean(dim=-1, keepdim=True) + eps)
+        return t * r.to(dtype) * gamma
 
-    W_new, b_new, h, eps = compute_fused_weights_rmsnorm(norm, linear)
-    fused = FusedRMSNormLinearInt8(W_new, b_new, h, eps)
+    def baseline_quantized():
+        return F.linear(norm(x), dequantize_int8(q_w, q_scale, dtype))
 
-    def baseline_quantized(t):
-        return F.linear(norm(t), dequantize_int8(q_w, q_scale, dtype))
-
-    def reference_fused_quantized(t):
-        w = dequantize_int8(fused.qweight, fused.w_scale, dtype)
-        variance = t.float().pow(2).mean(dim=-1, keepdim=True)
-        return F.linear(t * torch.rsqrt(variance + eps).to(dtype), w)
+    def reference_fused_quantized():
+        r = torch.rsqrt(x.float().pow(2).mean(dim=-1, keepdim=True) + eps)
+        return F.linear(x * r.to(dtype), dequantize_int8(fused.qweight, fused.w_scale, dtype))
 
     with torch.no_grad():
-        diff = (baseline_quantized(x).float() - fused(x).float()).abs()
-        diff_ref = (reference_fused_quantized(x).float() - fused(x).float()).abs()
-    baseline_ms = bench(baseline_quantized, x, args.warmup, args.iters, args.cuda_events)
-    ref_fused_ms = bench(reference_fused_quantized, x, args.warmup, args.iters, args.cuda_events)
-    fused_ms = bench(fused, x, args.warmup, args.iters, args.cuda_events)
+        ours = fused(x).float()
+        diff = (baseline_quantized().float() - ours).abs()
+        diff_ref = (reference_fused_quantized().float() - ours).abs()
+    baseline_ms = time_ms(baseline_quantized, args.warmup, args.iters)
+    ref_fused_ms = time_ms(reference_fused_quantized, args.warmup, args.iters)
+    fused_ms = time_ms(lambda: fused(x), args.warmup, args.iters)
     print(f"config={args.config} quantization=int8_per_output_channel")
     print(f"gpu={torch.cuda.get_device_name(0)} dtype={dtype}")
     print(f"shape=({tokens}, {hidden}) -> {out}")
