@@ -7,9 +7,9 @@ A step is one fused RMSNorm -> Linear call over one 512-token batch of the
 kimi_kv_b workload (x [512, 512] bf16, W_fused [16384, 512], out [512, 16384]).
 Steps rotate over enough (x, W, out) buffer sets that the working set is
 about twice the 126 MB L2, so every call streams W and out from/to HBM.  The
-K timed steps are replayed from CUDA graphs (one node per call), bracketed by a
-barrier and torch.cuda.synchronize() on both sides, timed with CUDA events on
-the launching stream.  That K-step window is repeated (at least 5 times and
+K timed steps are captured as one CUDA graph (one node per call) and replayed,
+bracketed by a barrier and torch.cuda.synchronize() on both sides, timed with
+CUDA events on the launching stream.  That K-step window is repeated (at least 5 times and
 until about 200 ms have been timed); each window's time is the max over ranks
 and the reported time is the median window.  With N > 1 (torchrun, one rank
 per GPU) each rank processes its own 512-token shard with its own weight
@@ -305,11 +305,12 @@ class Rotation:
 
 
 def time_windows(fns, steps, warmup, comm, min_total_ms=200.0, max_windows=2000):
-    """Times `steps` calls fns[i % S], replayed from CUDA graphs, as one window
-    bracketed by a barrier and a synchronize on both sides (CUDA events on the
-    launching stream).  The window is repeated (>= 5 times, until about
-    `min_total_ms` has been timed; every rank runs the same count).  Returns
-    (this rank's ms per window, max over ranks per window)."""
+    """Times `steps` calls fns[i % S] captured as ONE CUDA graph (one node per
+    call, back to back as a serving loop issues them), as one window bracketed
+    by a barrier and a synchronize on both sides (CUDA events on the launching
+    stream).  The window is repeated (>= 5 times, until about `min_total_ms`
+    has been timed; every rank runs the same count).  Returns (this rank's ms
+    per window, max over ranks per window)."""
     import torch
 
     S = len(fns)
@@ -320,19 +321,12 @@ def time_windows(fns, steps, warmup, comm, min_total_ms=200.0, max_windows=2000)
             f()
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
-    full = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(full):
-        for f in fns:
-            f()
-    rem = steps % S
-    part = None
-    if rem:
-        part = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(part):
-            for f in fns[:rem]:
-                f()
-    for _ in range(max(1, math.ceil(warmup / S))):
-        full.replay()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            fns[i % S]()
+    for _ in range(max(1, math.ceil(warmup / steps))):
+        graph.replay()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
@@ -341,10 +335,7 @@ def time_windows(fns, steps, warmup, comm, min_total_ms=200.0, max_windows=2000)
         comm.barrier()
         torch.cuda.synchronize()
         start.record()
-        for _ in range(steps // S):
-            full.replay()
-        if part is not None:
-            part.replay()
+        graph.replay()
         end.record()
         end.synchronize()
         torch.cuda.synchronize()
@@ -355,7 +346,7 @@ def time_windows(fns, steps, warmup, comm, min_total_ms=200.0, max_windows=2000)
     n = int(min(max_windows, max(5, math.ceil(min_total_ms / max(first, 1e-3)))))
     local = [window() for _ in range(n)]
     job = comm.max_(local)
-    del full, part
+    del graph
     return local, job
 
 
@@ -526,9 +517,10 @@ def run_ours(args):
             "timing": {"windows": len(job), "us_per_call": ms * 1e3 / args.steps,
                        "window_ms_max_over_ranks": spread(job),
                        "us_per_call_by_rank": spread(rank_us),
-                       "method": "CUDA graph replay of K calls per window, CUDA events on "
-                                 "the launching stream, barrier + synchronize around each "
-                                 "window; median over windows of the max over ranks",
+                       "method": "one CUDA graph of the K calls replayed per window, CUDA "
+                                 "events on the launching stream, barrier + synchronize "
+                                 "around each window; median over windows of the max over "
+                                 "ranks",
                        "l2": rot.describe()},
             "e2e": e2e,
             "gpu_launches": args.steps * len(job),

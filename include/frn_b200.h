@@ -63,6 +63,7 @@ extern "C" {
 #define FRN_KERNEL_WIDE_N192   12  /* SM pair, two accumulators: 256x(2*192)  */
 #define FRN_KERNEL_WIDE_N224   13  /* SM pair, two accumulators: 256x(2*224)  */
 #define FRN_KERNEL_WIDE_N256   14  /* SM pair, two accumulators: 256x(2*256)  */
+#define FRN_KERNEL_WIDE_N176   21  /* SM pair, two accumulators: 256x(2*176)  */
 
 /* Device error-word bits (frn_device_error). */
 #define FRN_DEVERR_WAIT_TIMEOUT  0x1u  /* an mbarrier wait ran out            */

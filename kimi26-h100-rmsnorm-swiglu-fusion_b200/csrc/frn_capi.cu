@@ -391,6 +391,7 @@ int frn_fused_rmsnorm_linear_ex(int dtype, const void* x, int64_t M, int64_t K,
     static const int bns[4] = {128, 192, 224, 256};
     return run_fused_linear_pair(p, PairChoice{bns[kernel - FRN_KERNEL_WIDE_N128], 2}, s);
   }
+  if (kernel == FRN_KERNEL_WIDE_N176) return run_fused_linear_pair(p, PairChoice{176, 2}, s);
   if (kernel == FRN_KERNEL_DECODE) {
     if (M > 128)
       return set_error(FRN_ERR_UNSUPPORTED, "the decode kernel takes M <= 128 (got %lld)",

@@ -70,7 +70,10 @@ struct PairCfg {
   static constexpr int WARP_RMS0 = 9;
   static constexpr int THREADS = 32 * (EPI_WARPS + 5 + RMS_WARPS);
   static_assert(STAGES % 2 == 0, "stages are split between two producers per operand");
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  // UMMA N for M = 256: a multiple of 16 up to 256.  The epilogue stores
+  // 64-column chunks and at most one 32-column tail per tile.
+  static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(TILE_N % 32 == 0, "tile width must be a multiple of 32 columns");
   static_assert(NACC == 1 || NACC == 2, "NACC");
   static_assert(NBUF * TILE_N <= 512, "TMEM has 512 columns");
   static_assert(B_BYTES % 1024 == 0, "stage buffers must stay 1024-aligned");
@@ -495,7 +498,7 @@ PairChoice choose_pair_tiling(int64_t M, int64_t N, int64_t K, int pairs, bool t
   const double mb = static_cast<double>((M + 255) / 256);
   const double nkb = static_cast<double>((K + 63) / 64);
   static const PairChoice cands[] = {{256, 1}, {224, 1}, {192, 1}, {160, 1}, {128, 1},
-                                     {256, 2}, {224, 2}, {192, 2}, {128, 2}};
+                                     {256, 2}, {224, 2}, {192, 2}, {176, 2}, {128, 2}};
   double best = 1e300;
   PairChoice pick = {256, 1};
   for (const PairChoice& c : cands) {
@@ -520,6 +523,7 @@ static int run_pair_t(const LinearProblem& pr, PairChoice c, cudaStream_t s) {
       case 256: return launch_pair<T, 256, 4, 2>(pr, s);
       case 224: return launch_pair<T, 224, 4, 2>(pr, s);
       case 192: return launch_pair<T, 192, 4, 2>(pr, s);
+      case 176: return launch_pair<T, 176, 4, 2>(pr, s);
       case 128: return launch_pair<T, 128, 6, 2>(pr, s);
       default: break;
     }

@@ -40,6 +40,7 @@ FRN_KERNEL_WIDE_N128 = 11
 FRN_KERNEL_WIDE_N192 = 12
 FRN_KERNEL_WIDE_N224 = 13
 FRN_KERNEL_WIDE_N256 = 14
+FRN_KERNEL_WIDE_N176 = 21
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
 PROTOTYPES = {

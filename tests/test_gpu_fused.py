@@ -54,7 +54,8 @@ def test_baseline_configs_full_size(config):
 ALL_KERNELS = [capi.FRN_KERNEL_TILE_N128, capi.FRN_KERNEL_TILE_N192, capi.FRN_KERNEL_TILE_N256,
                capi.FRN_KERNEL_PAIR_N128, capi.FRN_KERNEL_PAIR_N160, capi.FRN_KERNEL_PAIR_N192,
                capi.FRN_KERNEL_PAIR_N224, capi.FRN_KERNEL_PAIR_N256, capi.FRN_KERNEL_WIDE_N128,
-               capi.FRN_KERNEL_WIDE_N192, capi.FRN_KERNEL_WIDE_N224, capi.FRN_KERNEL_WIDE_N256]
+               capi.FRN_KERNEL_WIDE_N192, capi.FRN_KERNEL_WIDE_N224, capi.FRN_KERNEL_WIDE_N256,
+               capi.FRN_KERNEL_WIDE_N176]
 
 
 @pytest.mark.parametrize("kernel", ALL_KERNELS)
