@@ -714,7 +714,9 @@ def run_int8_stack(args, denominator_cuda, comm, device, rank, world, hbm_gbs, t
 
 
 def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
-    """µs/call of every BASELINE shape (ours vs the unfused cuBLAS path):
+    """µs/call of every BASELINE shape: ours, the unfused cuBLAS path, the
+    reference's fused path (cuBLAS F.linear + the in-place normalize epilogue)
+    and the cuBLAS GEMM alone;
     cold (rotating sets larger than L2; the roofline fraction uses this) and
     hot (one set reused, L2-warm where it fits)."""
     import torch
@@ -727,9 +729,23 @@ def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
                 for i in range(rot.S)]
         base = [(lambda i=i: unfused_torch(rot.xs[i], rot.gammas[i], rot.ws[i], EPS))
                 for i in range(rot.S)]
+        # The reference's fused path, F.linear(x, W_new) then the in-place
+        # normalize epilogue (src/fused_forward.py:182-191 there), with this
+        # library's normalize kernel; and the library GEMM alone.
+        zb = torch.zeros(N, dtype=torch.bfloat16, device=device)
+
+        def ref_path(i):
+            raw = torch.nn.functional.linear(rot.xs[i], rot.wf[i])
+            denominator_cuda.rmsnorm_normalize_512(rot.xs[i], raw, zb, K, EPS)
+
+        refp = [(lambda i=i: ref_path(i)) for i in range(rot.S)]
+        gemm = [(lambda i=i: torch.nn.functional.linear(rot.xs[i], rot.wf[i]))
+                for i in range(rot.S)]
         n = max(rot.S, min(steps, 4 * rot.S))
         t_ours = time_steps(ours, n, rot.S) * 1e3 / n
         t_base = time_steps(base, n, rot.S) * 1e3 / n
+        t_refp = time_steps(refp, n, rot.S) * 1e3 / n
+        t_gemm = time_steps(gemm, n, rot.S) * 1e3 / n
         # Hot: the same set every call, so whatever of it fits stays in L2.
         t_hot = time_steps(ours[:1], n, rot.S) * 1e3 / n
         fl, by = flops_of(M, K, N), bytes_of(M, K, N)
@@ -739,7 +755,10 @@ def run_sweep(denominator_cuda, device, hbm_gbs, tflops_peak, steps=400):
                      "roofline_us": round(roof_us, 3), "frac_of_roofline": round(roof_us / t_ours, 3),
                      "us_per_call_hot_l2": round(t_hot, 3),
                      "unfused_cublas_us": round(t_base, 3),
-                     "speedup_vs_unfused": round(t_base / t_ours, 3)}
+                     "speedup_vs_unfused": round(t_base / t_ours, 3),
+                     "reference_fused_path_us": round(t_refp, 3),
+                     "speedup_vs_reference_fused_path": round(t_refp / t_ours, 3),
+                     "cublas_gemm_only_us": round(t_gemm, 3)}
         del rot
         torch.cuda.empty_cache()
     res["int8_q_b"] = sweep_int8(denominator_cuda, device, hbm_gbs, tflops_peak, steps)
