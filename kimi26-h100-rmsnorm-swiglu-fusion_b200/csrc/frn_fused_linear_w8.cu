@@ -617,7 +617,9 @@ static int choose_w8_bn(int64_t M, int64_t N, int pairs) {
 
 template <typename T>
 static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
-  switch (choose_w8_bn(pr.M, pr.N, sm_count(0) / 2)) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
+  switch (choose_w8_bn(pr.M, pr.N, sm_count(dev) / 2)) {
     case 256: return launch_w8<T, 256, 4, 6>(pr, s);
     case 224: return launch_w8<T, 224, 5, 5>(pr, s);
     case 192: return launch_w8<T, 192, 5, 6>(pr, s);
