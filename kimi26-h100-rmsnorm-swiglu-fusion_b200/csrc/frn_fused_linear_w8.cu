@@ -210,6 +210,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
     // of the sequence with i % 2 == sel.
     if (lane == 0) {
       const uint32_t sel = warp == C::WARP_XLOAD ? 0u : 1u;
+      // While the preceding grid drains, pull this thread's share of the first
+      // ring of x tiles into L2.
+      if (t_begin < t_end) {
+        const int pm0 = (t_begin / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
+        for (int kb = static_cast<int>(sel); kb < nkb && kb < STAGES; kb += 2)
+          tma_prefetch_2d(&tmap_x, kb * C::BK, pm0);
+      }
       griddep_wait();
       uint32_t i = 0;
       bool ok = true;
@@ -229,6 +236,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
   } else if (warp == C::WARP_QLOAD) {
     // int8 half-tiles into their own ring, as far ahead as its QST slots go.
     if (lane == 0) {
+      if (t_begin < t_end) {  // the first ring of int8 tiles into L2 likewise
+        const int pn0 = (t_begin % p.num_n_blocks) * BN + rank * C::BN_HALF;
+        for (int kb = 0; kb < nkb && kb < QST; ++kb) tma_prefetch_2d(&tmap_q, kb * C::BK, pn0);
+      }
       griddep_wait();
       uint32_t i = 0;
       bool ok = true;
