@@ -147,6 +147,36 @@ int frn_fused_rmsnorm_linear_w8(int dtype,
                                 void* out, int64_t out_row_stride, void* stream);
 
 /*
+ * One int8-weight problem of frn_fused_rmsnorm_linear_w8_grouped: the
+ * arguments of frn_fused_rmsnorm_linear_w8 for one (x, wq) pair, same rules.
+ */
+typedef struct frn_w8_linear {
+  const void* x;
+  int64_t M, K, x_row_stride;
+  const int8_t* wq;
+  int64_t N, wq_row_stride;
+  const float* w_scale;
+  const void* bias; /* may be NULL */
+  void* out;
+  int64_t out_row_stride;
+} frn_w8_linear;
+
+/*
+ * nproblems (1 or 2) independent frn_fused_rmsnorm_linear_w8 problems of one
+ * dtype and eps in ONE launch -- e.g. an MLA layer's q_b and kv_b, which read
+ * different inputs.  Each SM pair runs its share of both problems' tiles
+ * back to back, so one problem's mainloop overlaps the other's last epilogue
+ * and the launch's fixed cost is paid once.  That pays off while each
+ * problem has at most 256 rows; with more, the two run as consecutive
+ * launches.  No output may alias an input of either problem.  Same results
+ * (bit for bit) as two frn_fused_rmsnorm_linear_w8 calls.
+ * No counterpart in the reference, which launches each projection on its
+ * own (src/benchmark_kimi26_quantized.py:102-106).
+ */
+int frn_fused_rmsnorm_linear_w8_grouped(int dtype, const frn_w8_linear* problems,
+                                        int nproblems, float eps, void* stream);
+
+/*
  * Symmetric per-output-channel int8 quantization of a (gamma-folded) weight
  * w[N,K] (dtype fp32 / fp16 / bf16):
  *     scale[n] = max(max_k |w[n,k]|, 1e-8) / 127        (fp32)

@@ -284,9 +284,11 @@ at::Tensor fused_rmsnorm_linear(const at::Tensor& x_in, const at::Tensor& w,
   return o;
 }
 
-at::Tensor fused_rmsnorm_linear_w8(const at::Tensor& x_in, const at::Tensor& qweight,
-                                   const at::Tensor& w_scale, const c10::optional<at::Tensor>& b_new,
-                                   double eps, c10::optional<at::Tensor> out) {
+// Checks one int8 problem's tensors and fills its C-ABI descriptor; `keep`
+// holds the contiguous copies (if any) alive until the launch.
+static frn_w8_linear prepare_w8(const at::Tensor& x_in, const at::Tensor& qweight,
+                                const at::Tensor& w_scale, const c10::optional<at::Tensor>& b_new,
+                                const c10::optional<at::Tensor>& out, std::vector<at::Tensor>& keep) {
   TORCH_CHECK(x_in.dim() == 2 && qweight.dim() == 2, "x and qweight must be 2D");
   TORCH_CHECK(x_in.is_cuda() && qweight.is_cuda() && w_scale.is_cuda() &&
                   (!b_new || b_new->is_cuda()),
@@ -301,24 +303,67 @@ at::Tensor fused_rmsnorm_linear_w8(const at::Tensor& x_in, const at::Tensor& qwe
   const at::Tensor q = qweight.stride(1) == 1 ? qweight : qweight.contiguous();
   const at::Tensor sc = w_scale.contiguous();
   const int64_t M = x.size(0), K = x.size(1), N = q.size(0);
-  at::Tensor b;
   const void* bptr = nullptr;
   if (b_new && b_new->defined()) {
     TORCH_CHECK(b_new->scalar_type() == x.scalar_type() && b_new->numel() == N,
                 "b_new must share x's dtype and have qweight.size(0) elements");
-    b = b_new->contiguous();
-    bptr = b.data_ptr();
+    keep.push_back(b_new->contiguous());
+    bptr = keep.back().data_ptr();
   }
   at::Tensor o = (out && out->defined()) ? *out : at::empty({M, N}, x.options());
   TORCH_CHECK(o.dim() == 2 && o.size(0) == M && o.size(1) == N && o.stride(1) == 1,
               "out must be [M, N] with unit inner stride");
+  keep.push_back(x);
+  keep.push_back(q);
+  keep.push_back(sc);
+  keep.push_back(o);
+  frn_w8_linear d;
+  d.x = x.data_ptr();
+  d.M = M;
+  d.K = K;
+  d.x_row_stride = x.stride(0);
+  d.wq = static_cast<const int8_t*>(q.data_ptr());
+  d.N = N;
+  d.wq_row_stride = q.stride(0);
+  d.w_scale = sc.data_ptr<float>();
+  d.bias = bptr;
+  d.out = o.data_ptr();
+  d.out_row_stride = o.stride(0);
+  return d;
+}
+
+at::Tensor fused_rmsnorm_linear_w8(const at::Tensor& x_in, const at::Tensor& qweight,
+                                   const at::Tensor& w_scale, const c10::optional<at::Tensor>& b_new,
+                                   double eps, c10::optional<at::Tensor> out) {
+  std::vector<at::Tensor> keep;
+  const frn_w8_linear d = prepare_w8(x_in, qweight, w_scale, b_new, out, keep);
+  const at::Tensor& x = keep[keep.size() - 4];
   const c10::cuda::CUDAGuard guard(x.device());
-  check_rc(frn_fused_rmsnorm_linear_w8(dtype_code(x), x.data_ptr(), M, K, x.stride(0),
-                                       static_cast<const int8_t*>(q.data_ptr()), N, q.stride(0),
-                                       sc.data_ptr<float>(), bptr, static_cast<float>(eps),
-                                       o.data_ptr(), o.stride(0), stream_of(x)),
+  check_rc(frn_fused_rmsnorm_linear_w8(dtype_code(x), d.x, d.M, d.K, d.x_row_stride, d.wq, d.N,
+                                       d.wq_row_stride, d.w_scale, d.bias,
+                                       static_cast<float>(eps), d.out, d.out_row_stride,
+                                       stream_of(x)),
            "fused_rmsnorm_linear_w8");
-  return o;
+  return keep.back();
+}
+
+// Two independent int8 problems (e.g. a layer's q_b and kv_b) in one launch.
+std::tuple<at::Tensor, at::Tensor> fused_rmsnorm_linear_w8_grouped(
+    const at::Tensor& x_a, const at::Tensor& qweight_a, const at::Tensor& w_scale_a,
+    const c10::optional<at::Tensor>& b_a, const at::Tensor& x_b, const at::Tensor& qweight_b,
+    const at::Tensor& w_scale_b, const c10::optional<at::Tensor>& b_b, double eps,
+    c10::optional<at::Tensor> out_a, c10::optional<at::Tensor> out_b) {
+  TORCH_CHECK(x_a.scalar_type() == x_b.scalar_type() && x_a.device() == x_b.device(),
+              "grouped problems must share x's dtype and device");
+  std::vector<at::Tensor> keep_a, keep_b;
+  frn_w8_linear d[2];
+  d[0] = prepare_w8(x_a, qweight_a, w_scale_a, b_a, out_a, keep_a);
+  d[1] = prepare_w8(x_b, qweight_b, w_scale_b, b_b, out_b, keep_b);
+  const c10::cuda::CUDAGuard guard(x_a.device());
+  check_rc(frn_fused_rmsnorm_linear_w8_grouped(dtype_code(x_a), d, 2, static_cast<float>(eps),
+                                               stream_of(x_a)),
+           "fused_rmsnorm_linear_w8_grouped");
+  return {keep_a.back(), keep_b.back()};
 }
 
 std::tuple<at::Tensor, at::Tensor> quantize_int8_per_channel(const at::Tensor& w_in) {
@@ -405,6 +450,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "int8 weights: rsqrt(mean(x^2)+eps)[:,None] * w_scale * (x @ qweight.T) + b_new",
         py::arg("x"), py::arg("qweight"), py::arg("w_scale"), py::arg("b_new") = py::none(),
         py::arg("eps") = 1e-6, py::arg("out") = py::none());
+  m.def("fused_rmsnorm_linear_w8_grouped", &fused_rmsnorm_linear_w8_grouped,
+        "two independent int8 fused RMSNorm -> Linear problems in one launch",
+        py::arg("x_a"), py::arg("qweight_a"), py::arg("w_scale_a"), py::arg("b_a"),
+        py::arg("x_b"), py::arg("qweight_b"), py::arg("w_scale_b"), py::arg("b_b"),
+        py::arg("eps") = 1e-6, py::arg("out_a") = py::none(), py::arg("out_b") = py::none());
   m.def("quantize_int8_per_channel", &quantize_int8_per_channel,
         "Symmetric per-output-channel int8 quantization on the GPU -> (qweight, w_scale)",
         py::arg("weight"));

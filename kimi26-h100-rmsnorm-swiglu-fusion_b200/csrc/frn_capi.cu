@@ -464,10 +464,10 @@ int frn_fused_rmsnorm_linear(int dtype, const void* x, int64_t M, int64_t K, int
                                      FRN_KERNEL_AUTO, stream);
 }
 
-int frn_fused_rmsnorm_linear_w8(int dtype, const void* x, int64_t M, int64_t K,
-                                int64_t x_row_stride, const int8_t* wq, int64_t N,
-                                int64_t wq_row_stride, const float* w_scale, const void* bias,
-                                float eps, void* out, int64_t out_row_stride, void* stream) {
+// Argument checks of one int8-weight problem (both entry points).
+static int validate_w8(int dtype, const void* x, int64_t M, int64_t K, int64_t x_row_stride,
+                       const int8_t* wq, int64_t N, int64_t wq_row_stride, const float* w_scale,
+                       const void* bias, const void* out, int64_t out_row_stride) {
   if (dtype != FRN_DTYPE_BF16 && dtype != FRN_DTYPE_F16)
     return set_error(FRN_ERR_UNSUPPORTED, "int8-weight RMSNorm+Linear takes bf16 or fp16 x");
   if (M < 0 || N <= 0 || K <= 0)
@@ -487,9 +487,39 @@ int frn_fused_rmsnorm_linear_w8(int dtype, const void* x, int64_t M, int64_t K,
   if (!aligned16(x) || !aligned16(wq) || !aligned16(w_scale) || !aligned16(out) ||
       (bias && !aligned16(bias)))
     return set_error(FRN_ERR_MISALIGNED, "x, wq, w_scale, bias and out must be 16-byte aligned");
+  return FRN_OK;
+}
+
+int frn_fused_rmsnorm_linear_w8(int dtype, const void* x, int64_t M, int64_t K,
+                                int64_t x_row_stride, const int8_t* wq, int64_t N,
+                                int64_t wq_row_stride, const float* w_scale, const void* bias,
+                                float eps, void* out, int64_t out_row_stride, void* stream) {
+  const int rc = validate_w8(dtype, x, M, K, x_row_stride, wq, N, wq_row_stride, w_scale, bias,
+                             out, out_row_stride);
+  if (rc || M == 0) return rc;
   W8Problem p{dtype, x, M, K, x_row_stride, wq, N, wq_row_stride, w_scale, bias, eps, out,
               out_row_stride};
   return run_fused_linear_w8(p, static_cast<cudaStream_t>(stream));
+}
+
+int frn_fused_rmsnorm_linear_w8_grouped(int dtype, const frn_w8_linear* problems,
+                                        int nproblems, float eps, void* stream) {
+  if (!problems || nproblems < 1 || nproblems > 2)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "grouped int8 call takes 1 or 2 problems (got %d)",
+                     nproblems);
+  W8Problem ps[2];
+  int n = 0;
+  for (int j = 0; j < nproblems; ++j) {
+    const frn_w8_linear& q = problems[j];
+    const int rc = validate_w8(dtype, q.x, q.M, q.K, q.x_row_stride, q.wq, q.N, q.wq_row_stride,
+                               q.w_scale, q.bias, q.out, q.out_row_stride);
+    if (rc) return rc;
+    if (q.M == 0) continue;  // nothing to do for this one
+    ps[n++] = W8Problem{dtype, q.x, q.M, q.K, q.x_row_stride, q.wq, q.N, q.wq_row_stride,
+                        q.w_scale, q.bias, eps, q.out, q.out_row_stride};
+  }
+  if (n == 0) return FRN_OK;
+  return run_fused_linear_w8_group(ps, n, static_cast<cudaStream_t>(stream));
 }
 
 int frn_quantize_int8_per_channel(int dtype, const void* w, int64_t N, int64_t K,

@@ -33,6 +33,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "frn_internal.h"
 #include "frn_ptx.cuh"
@@ -49,6 +50,32 @@ struct W8Params {
   int64_t out_row_stride;
   uint64_t timeout_ns;
 };
+
+// One launch serves one or two independent problems (same x type and tile
+// width, e.g. an MLA layer's q_b and kv_b, which read different inputs): each
+// pair takes a balanced contiguous run of each problem's tiles (problem 1's
+// runs in reverse pair order, so a pair with an extra problem-0 tile gets one
+// fewer of problem 1), problem 0's first.  The rings, the accumulators and
+// the inv_rms buffers carry on from one problem to the next, so the second
+// problem's mainloop overlaps the first one's last epilogue.
+struct W8Group {
+  W8Params p[2];
+  int32_t nprob;
+};
+
+struct W8Maps {
+  CUtensorMap x[2], q[2], out[2], out_half[2];
+};
+
+// Tiles [tb, te) of problem j for pair `pair` of `npairs`.
+__device__ __forceinline__ void w8_tile_range(const W8Params& q, int j, int pair, int npairs,
+                                              int& tb, int& te) {
+  const int tiles = q.num_m_blocks * q.num_n_blocks;
+  const int pr = j == 0 ? pair : npairs - 1 - pair;
+  const int base = tiles / npairs, rem = tiles % npairs;
+  tb = pr * base + min(pr, rem);
+  te = tb + base + (pr < rem ? 1 : 0);
+}
 
 template <int BN, int STAGES, int QST>
 struct W8Cfg {
@@ -122,11 +149,8 @@ __device__ __forceinline__ void widen_s8x4<__half>(uint32_t w, uint32_t& o01, ui
 
 template <typename T, int BN, int STAGES, int QST>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QST>::THREADS, 1)
-    fused_rmsnorm_linear_w8_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                                   const __grid_constant__ CUtensorMap tmap_q,
-                                   const __grid_constant__ CUtensorMap tmap_out,
-                                   const __grid_constant__ CUtensorMap tmap_out_half,
-                                   const W8Params p) {
+    fused_rmsnorm_linear_w8_kernel(const __grid_constant__ W8Maps maps,
+                                   const __grid_constant__ W8Group grp) {
   using C = W8Cfg<BN, STAGES, QST>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -154,10 +178,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
   const uint32_t num_pairs = gridDim.x >> 1;
 
   if (warp == C::WARP_XLOAD && lane == 0) {
-    prefetch_tmap(&tmap_x);
-    prefetch_tmap(&tmap_q);
-    prefetch_tmap(&tmap_out);
-    if (C::HALF_TAIL) prefetch_tmap(&tmap_out_half);
+    for (int j = 0; j < grp.nprob; ++j) {
+      prefetch_tmap(&maps.x[j]);
+      prefetch_tmap(&maps.q[j]);
+      prefetch_tmap(&maps.out[j]);
+      if (C::HALF_TAIL) prefetch_tmap(&maps.out_half[j]);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&conv[s], 1);  // even CTA's converter arrives; odd CTA's sends 4 tx bytes
@@ -190,15 +216,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Contiguous m-block-major tile run per pair (inv_rms once per run).
-  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
-  const int tiles_base = num_tiles / static_cast<int>(num_pairs);
-  const int tiles_rem = num_tiles % static_cast<int>(num_pairs);
-  const int t_begin = static_cast<int>(pair) * tiles_base +
-                      min(static_cast<int>(pair), tiles_rem);
-  const int t_end = t_begin + tiles_base + (static_cast<int>(pair) < tiles_rem ? 1 : 0);
-  const int nkb = p.num_k_blocks;
-  const uint64_t to = p.timeout_ns;
+  // This pair's contiguous m-block-major run of each problem's tiles
+  // (inv_rms once per run), and how many tiles and k-blocks that is in all.
+  int tb[2] = {0, 0}, te[2] = {0, 0};
+  int pair_tiles = 0, pair_kbs = 0;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    if (j < grp.nprob) {
+      w8_tile_range(grp.p[j], j, static_cast<int>(pair), static_cast<int>(num_pairs), tb[j], te[j]);
+      pair_tiles += te[j] - tb[j];
+      pair_kbs += (te[j] - tb[j]) * grp.p[j].num_k_blocks;
+    }
+  }
+  const int j0 = te[0] > tb[0] ? 0 : 1;  // the problem of this pair's first tile
+  const int tb_first = j0 == 0 ? tb[0] : tb[1], te_first = j0 == 0 ? te[0] : te[1];
+  const uint64_t to = grp.p[0].timeout_ns;
   // Let the next kernel in the stream get scheduled now: its CTAs take SMs as
   // ours retire and run their set-up while we finish; its griddepcontrol.wait
   // still orders all of its global accesses after this whole grid.
@@ -212,44 +244,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
       const uint32_t sel = warp == C::WARP_XLOAD ? 0u : 1u;
       // While the preceding grid drains, pull this thread's share of the first
       // ring of x tiles into L2.
-      if (t_begin < t_end) {
-        const int pm0 = (t_begin / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
-        for (int kb = static_cast<int>(sel); kb < nkb && kb < STAGES; kb += 2)
-          tma_prefetch_2d(&tmap_x, kb * C::BK, pm0);
+      if (tb_first < te_first) {
+        const W8Params& pf = grp.p[j0];
+        const int pm0 = (tb_first / pf.num_n_blocks) * 2 * C::BM + rank * C::BM;
+        for (int kb = static_cast<int>(sel); kb < pf.num_k_blocks && kb < STAGES; kb += 2)
+          tma_prefetch_2d(&maps.x[j0], kb * C::BK, pm0);
       }
       griddep_wait();
       uint32_t i = 0;
       bool ok = true;
-      for (int t = t_begin; t < t_end && ok; ++t) {
-        const int m0 = (t / p.num_n_blocks) * 2 * C::BM + rank * C::BM;
-        for (int kb = 0; kb < nkb; ++kb, ++i) {
-          if ((i & 1u) != sel) continue;
-          const uint32_t s = i % STAGES, ph = (i / STAGES) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, to)) { ok = false; break; }
-          const uint32_t leader_full = mapa_shared(smem_addr(&full[s]), 0);
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], C::PAIR_A_TX);
-          tma_load_2d_pair(smem + C::OFF_A + s * C::A_BYTES, &tmap_x, leader_full, kb * C::BK,
-                           m0);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const W8Params& pj = grp.p[j];
+        for (int t = tb[j]; t < te[j] && ok; ++t) {
+          const int m0 = (t / pj.num_n_blocks) * 2 * C::BM + rank * C::BM;
+          for (int kb = 0; kb < pj.num_k_blocks; ++kb, ++i) {
+            if ((i & 1u) != sel) continue;
+            const uint32_t s = i % STAGES, ph = (i / STAGES) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, to)) { ok = false; break; }
+            const uint32_t leader_full = mapa_shared(smem_addr(&full[s]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], C::PAIR_A_TX);
+            tma_load_2d_pair(smem + C::OFF_A + s * C::A_BYTES, &maps.x[j], leader_full,
+                             kb * C::BK, m0);
+          }
         }
       }
     }
   } else if (warp == C::WARP_QLOAD) {
     // int8 half-tiles into their own ring, as far ahead as its QST slots go.
     if (lane == 0) {
-      if (t_begin < t_end) {  // the first ring of int8 tiles into L2 likewise
-        const int pn0 = (t_begin % p.num_n_blocks) * BN + rank * C::BN_HALF;
-        for (int kb = 0; kb < nkb && kb < QST; ++kb) tma_prefetch_2d(&tmap_q, kb * C::BK, pn0);
+      if (tb_first < te_first) {  // the first ring of int8 tiles into L2 likewise
+        const W8Params& pf = grp.p[j0];
+        const int pn0 = (tb_first % pf.num_n_blocks) * BN + rank * C::BN_HALF;
+        for (int kb = 0; kb < pf.num_k_blocks && kb < QST; ++kb)
+          tma_prefetch_2d(&maps.q[j0], kb * C::BK, pn0);
       }
       griddep_wait();
       uint32_t i = 0;
       bool ok = true;
-      for (int t = t_begin; t < t_end && ok; ++t) {
-        const int n0 = (t % p.num_n_blocks) * BN + rank * C::BN_HALF;
-        for (int kb = 0; kb < nkb; ++kb, ++i) {
-          const uint32_t qs = i % QST, qph = (i / QST) & 1u;
-          if (!mbar_wait(&qempty[qs], qph ^ 1u, abort_flag, to)) { ok = false; break; }
-          mbar_arrive_expect_tx(&qfull[qs], C::Q_BYTES);
-          tma_load_2d(smem + C::OFF_Q + qs * C::Q_BYTES, &tmap_q, &qfull[qs], kb * C::BK, n0);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const W8Params& pj = grp.p[j];
+        for (int t = tb[j]; t < te[j] && ok; ++t) {
+          const int n0 = (t % pj.num_n_blocks) * BN + rank * C::BN_HALF;
+          for (int kb = 0; kb < pj.num_k_blocks; ++kb, ++i) {
+            const uint32_t qs = i % QST, qph = (i / QST) & 1u;
+            if (!mbar_wait(&qempty[qs], qph ^ 1u, abort_flag, to)) { ok = false; break; }
+            mbar_arrive_expect_tx(&qfull[qs], C::Q_BYTES);
+            tma_load_2d(smem + C::OFF_Q + qs * C::Q_BYTES, &maps.q[j], &qfull[qs], kb * C::BK,
+                        n0);
+          }
         }
       }
     }
@@ -259,9 +303,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
       uint32_t stage = 0, phase = 0;
       int i = 0;
       bool ok = true;
-      for (int t = t_begin; t < t_end && ok; ++t, ++i) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+       const int nkb = grp.p[j].num_k_blocks;
+       for (int t = tb[j]; t < te[j] && ok; ++t, ++i) {
         const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
-        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) break;
+        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < nkb; ++kb) {
@@ -285,6 +335,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
         }
         if (!ok) break;
         umma_commit_pair_mc(&tmem_full[acc], 0x3);
+       }
       }
       umma_commit_pair_mc(drain, 0x1);
       uint32_t zero = 0;
@@ -299,7 +350,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
     const uint32_t leader_conv0 = mapa_shared(smem_addr(&conv[0]), 0);
     const uint32_t leader_sink = mapa_shared(smem_addr(tmem_slot + 2), 0);
     const uint32_t q0 = smem_addr(smem + C::OFF_Q), b0 = smem_addr(smem + C::OFF_B);
-    const uint32_t total = static_cast<uint32_t>((t_end - t_begin) * nkb);
+    const uint32_t total = static_cast<uint32_t>(pair_kbs);
     for (uint32_t i = cw; i < total; i += C::CONV_WARPS) {
       const uint32_t qs = i % QST, qph = (i / QST) & 1u;
       const uint32_t stage = i % STAGES, phase = (i / STAGES) & 1u;
@@ -344,16 +395,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
     }
   } else if (warp >= C::WARP_RMS0) {
     const int r = static_cast<int>(threadIdx.x) - C::WARP_RMS0 * 32;
-    const float inv_k = 1.0f / static_cast<float>(p.K);
     uint32_t stage = 0, phase = 0;
-    int gen = -1, cur_m = -1;
+    int gen = -1;
     bool ok = true;
-    for (int t = t_begin; t < t_end && ok; ++t) {
-      const int mb = t / p.num_n_blocks;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+     const W8Params& pj = grp.p[j];
+     int cur_m = -1;
+     for (int t = tb[j]; t < te[j] && ok; ++t) {
+      const int mb = t / pj.num_n_blocks;
       const bool first = (mb != cur_m);
       if (first) { ++gen; cur_m = mb; }
       float ss0 = 0.f, ss1 = 0.f;
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; kb < pj.num_k_blocks; ++kb) {
         if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
         if (first) {
           const uint32_t row = smem_addr(smem + C::OFF_A + stage * C::A_BYTES) + r * 128;
@@ -374,31 +428,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
       }
       if (!ok || !first) continue;
       const uint32_t g = static_cast<uint32_t>(gen);
-      if (!mbar_wait(&rms_empty[g & 1], ((g >> 1) & 1) ^ 1u, abort_flag, to)) break;
-      rms_buf[(g & 1) * C::BM + r] = rsqrtf((ss0 + ss1) * inv_k + p.eps);
+      if (!mbar_wait(&rms_empty[g & 1], ((g >> 1) & 1) ^ 1u, abort_flag, to)) {
+        ok = false;
+        break;
+      }
+      const float inv_k = 1.0f / static_cast<float>(pj.K);
+      rms_buf[(g & 1) * C::BM + r] = rsqrtf((ss0 + ss1) * inv_k + pj.eps);
       __syncwarp();
       if (lane == 0) mbar_arrive(&rms_full[g & 1]);
+     }
     }
   } else {
     // Epilogue warps 0-3 (as in the bf16 pair kernel, plus scale[n]).
     const uint32_t q = warp;
-    const bool has_bias = p.bias != nullptr;
-    const T* bias = static_cast<const T*>(p.bias);
     const uint32_t leader_tmem_empty0 = mapa_shared(smem_addr(&tmem_empty[0]), 0);
     const uint32_t scl = smem_addr(smem + C::OFF_SCL + q * BN * 4);  // this warp's scale[n0 ..)
     griddep_wait();
     uint32_t nst = 0;  // chunks this warp has staged: staging buffer nst & 1
     int i = 0;
-    int gen = -1, cur_m = -1;
+    int gen = -1;
     float inv_rms = 0.f;
-    for (int t = t_begin; t < t_end; ++t, ++i) {
+    bool ok = true;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+     const W8Params& pj = grp.p[j];
+     int cur_m = -1;
+     for (int t = tb[j]; t < te[j] && ok; ++t, ++i) {
+      const bool has_bias = pj.bias != nullptr;
+      const T* bias = static_cast<const T*>(pj.bias);
       const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
-      const int mb = t / p.num_n_blocks;
+      const int mb = t / pj.num_n_blocks;
       const int row_base = mb * 2 * C::BM + rank * C::BM + q * 32;
-      const int n0 = (t % p.num_n_blocks) * BN;
+      const int n0 = (t % pj.num_n_blocks) * BN;
       const bool first = (mb != cur_m);
-      const bool last = (t + 1 >= t_end) || ((t + 1) / p.num_n_blocks != mb);
-      const bool reuse_acc = t + 2 < t_end;
+      const bool last = (t + 1 >= te[j]) || ((t + 1) / pj.num_n_blocks != mb);
+      const bool reuse_acc = i + 2 < pair_tiles;  // a later tile (of either problem) uses acc
       if (first) { ++gen; cur_m = mb; }
       const uint32_t g = static_cast<uint32_t>(gen);
       // The tile's column scales (0 past N) into this warp's slice; N % 8 == 0,
@@ -406,13 +470,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
       for (int c4 = static_cast<int>(lane); c4 < BN / 4; c4 += 32) {
         const int col = n0 + c4 * 4;
         uint4 sv = make_uint4(0u, 0u, 0u, 0u);
-        if (col < p.N) sv = ld_global_nc_v4(p.scale + col);
+        if (col < pj.N) sv = ld_global_nc_v4(pj.scale + col);
         st_shared_v4(scl + c4 * 16, sv.x, sv.y, sv.z, sv.w);
       }
       __syncwarp();
-      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) break;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) {
+        ok = false;
+        break;
+      }
       if (first) {
-        if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) break;
+        if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) {
+          ok = false;
+          break;
+        }
         inv_rms = rms_buf[(g & 1) * C::BM + q * 32 + lane];
       }
       tc_fence_after();
@@ -428,10 +498,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
         uint4 bv[8];
         if (has_bias) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            bv[j] = (col0 + j * 8 < p.N && !(half && j >= 4))
-                        ? ld_global_nc_v4(bias + col0 + j * 8)
-                        : make_uint4(0u, 0u, 0u, 0u);
+          for (int c8 = 0; c8 < 8; ++c8)
+            bv[c8] = (col0 + c8 * 8 < pj.N && !(half && c8 >= 4))
+                         ? ld_global_nc_v4(bias + col0 + c8 * 8)
+                         : make_uint4(0u, 0u, 0u, 0u);
         }
         uint32_t v[64];
         tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
@@ -458,10 +528,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(half ? &tmap_out_half : &tmap_out, sbp, col0, row_base);
+          tma_store_2d(half ? &maps.out_half[j] : &maps.out[j], sbp, col0, row_base);
           bulk_commit_group();
         }
       }
+     }
     }
     if (lane == 0) bulk_wait_group_read<0>();
   }
@@ -530,7 +601,7 @@ int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws
 // ------------------------------------------------------------------ host side
 
 template <typename T, int BN, int STAGES, int QST>
-static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
+static int launch_w8(const W8Problem* prs, int nprob, cudaStream_t stream) {
   using C = W8Cfg<BN, STAGES, QST>;
   auto kern = fused_rmsnorm_linear_w8_kernel<T, BN, STAGES, QST>;
   int dev = 0;
@@ -561,39 +632,49 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
   }
   const int pairs_avail = dev < kMaxDevices ? max_pairs[dev] : sm_count(dev) / 2;
   const CUtensorMapDataType dt = Elem16<T>::kTmaType;
-  CUtensorMap tx, tq;
-  int rc = encode_tmap_2d(&tx, dt, 2, pr.x, pr.K, pr.M, pr.x_row_stride, C::BK, C::BM,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = encode_tmap_2d(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, pr.wq, pr.K, pr.N, pr.wq_row_stride,
-                      C::BK, C::BN_HALF, CU_TENSOR_MAP_SWIZZLE_64B);
-  if (rc) return rc;
-  CUtensorMap to, toh;
-  rc = encode_tmap_2d(&to, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 64, 32,
-                      CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  if (C::HALF_TAIL) {
-    rc = encode_tmap_2d(&toh, dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 32, 32,
-                        CU_TENSOR_MAP_SWIZZLE_64B);
+  W8Maps maps;
+  W8Group grp;
+  memset(&maps, 0, sizeof(maps));
+  memset(&grp, 0, sizeof(grp));
+  grp.nprob = nprob;
+  int max_tiles = 0;
+  for (int j = 0; j < nprob; ++j) {
+    const W8Problem& pr = prs[j];
+    int rc = encode_tmap_2d(&maps.x[j], dt, 2, pr.x, pr.K, pr.M, pr.x_row_stride, C::BK, C::BM,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-  } else {
-    toh = to;
+    rc = encode_tmap_2d(&maps.q[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, pr.wq, pr.K, pr.N,
+                        pr.wq_row_stride, C::BK, C::BN_HALF, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+    rc = encode_tmap_2d(&maps.out[j], dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 64, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (C::HALF_TAIL) {
+      rc = encode_tmap_2d(&maps.out_half[j], dt, 2, pr.out, pr.N, pr.M, pr.out_row_stride, 32, 32,
+                          CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc) return rc;
+    } else {
+      maps.out_half[j] = maps.out[j];
+    }
+    W8Params& p = grp.p[j];
+    p.M = static_cast<int32_t>(pr.M);
+    p.N = static_cast<int32_t>(pr.N);
+    p.K = static_cast<int32_t>(pr.K);
+    p.num_m_blocks = static_cast<int32_t>((pr.M + 2 * C::BM - 1) / (2 * C::BM));
+    p.num_n_blocks = static_cast<int32_t>((pr.N + BN - 1) / BN);
+    p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
+    p.eps = pr.eps;
+    p.scale = pr.scale;
+    p.bias = pr.bias;
+    p.out = pr.out;
+    p.out_row_stride = pr.out_row_stride;
+    p.timeout_ns = wait_timeout_ns();
+    const int tiles = p.num_m_blocks * p.num_n_blocks;
+    if (tiles > max_tiles) max_tiles = tiles;
   }
-  W8Params p;
-  p.M = static_cast<int32_t>(pr.M);
-  p.N = static_cast<int32_t>(pr.N);
-  p.K = static_cast<int32_t>(pr.K);
-  p.num_m_blocks = static_cast<int32_t>((pr.M + 2 * C::BM - 1) / (2 * C::BM));
-  p.num_n_blocks = static_cast<int32_t>((pr.N + BN - 1) / BN);
-  p.num_k_blocks = static_cast<int32_t>((pr.K + C::BK - 1) / C::BK);
-  p.eps = pr.eps;
-  p.scale = pr.scale;
-  p.bias = pr.bias;
-  p.out = pr.out;
-  p.out_row_stride = pr.out_row_stride;
-  p.timeout_ns = wait_timeout_ns();
-  const int tiles = p.num_m_blocks * p.num_n_blocks;
-  const int pairs = tiles < pairs_avail ? tiles : pairs_avail;
+  // As many pairs as the larger problem has tiles (the smaller one's runs
+  // then sit on the last pairs, away from the larger one's extra tiles).
+  const int pairs = max_tiles < pairs_avail ? max_tiles : pairs_avail;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(C::THREADS);
@@ -604,44 +685,66 @@ static int launch_w8(const W8Problem& pr, cudaStream_t stream) {
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tx, tq, to, toh, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, grp);
   if (e != cudaSuccess) return set_cuda_error("launch fused_rmsnorm_linear_w8", e);
   return 0;
 }
 
-// Tile width for the int8 kernel: the fewest tensor-core columns on the
-// busiest pair, ceil(tiles / pairs) * bn (ties to the wider tile); 256 leaves
-// room for only six int8 slots instead of eight.
-static int choose_w8_bn(int64_t M, int64_t N, int pairs) {
+// Tile width for the int8 kernel: the fewest tensor-core MACs on the busiest
+// pair, sum over the problems of ceil(tiles / pairs) * bn * k-blocks (ties to
+// the wider tile); 256 leaves room for only six int8 slots instead of eight.
+static int choose_w8_bn(const W8Problem* prs, int nprob, int pairs) {
   static const int cands[] = {256, 224, 192, 128};
-  const int64_t mb = (M + 255) / 256;
   int pick = 256;
   double best = 1e300;
   for (int bn : cands) {
-    const int64_t tiles = mb * ((N + bn - 1) / bn);
-    const double cost = static_cast<double>((tiles + pairs - 1) / pairs) * bn *
-                        (bn == 256 ? 1.1 : 1.0);  // the shallower ring
+    double cost = 0.0;
+    for (int j = 0; j < nprob; ++j) {
+      const int64_t mb = (prs[j].M + 255) / 256;
+      const int64_t tiles = mb * ((prs[j].N + bn - 1) / bn);
+      const int64_t nkb = (prs[j].K + 63) / 64;
+      cost += static_cast<double>((tiles + pairs - 1) / pairs) * bn * static_cast<double>(nkb);
+    }
+    cost *= (bn == 256 ? 1.1 : 1.0);  // the shallower ring
     if (cost < best * 0.999) { best = cost; pick = bn; }
   }
   return pick;
 }
 
 template <typename T>
-static int run_w8_t(const W8Problem& pr, cudaStream_t s) {
+static int run_w8_t(const W8Problem* prs, int nprob, cudaStream_t s) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return set_cuda_error("cudaGetDevice");
-  switch (choose_w8_bn(pr.M, pr.N, sm_count(dev) / 2)) {
-    case 256: return launch_w8<T, 256, 4, 6>(pr, s);
-    case 224: return launch_w8<T, 224, 5, 5>(pr, s);
-    case 192: return launch_w8<T, 192, 5, 6>(pr, s);
-    default: return launch_w8<T, 128, 6, 8>(pr, s);
+  switch (choose_w8_bn(prs, nprob, sm_count(dev) / 2)) {
+    case 256: return launch_w8<T, 256, 4, 6>(prs, nprob, s);
+    case 224: return launch_w8<T, 224, 5, 5>(prs, nprob, s);
+    case 192: return launch_w8<T, 192, 5, 6>(prs, nprob, s);
+    default: return launch_w8<T, 128, 6, 8>(prs, nprob, s);
   }
 }
 
+int run_fused_linear_w8_group(const W8Problem* prs, int nprob, cudaStream_t s) {
+  if (nprob < 1 || nprob > 2)
+    return set_error(FRN_ERR_INVALID_ARGUMENT, "one launch takes 1 or 2 problems (got %d)", nprob);
+  for (int j = 1; j < nprob; ++j)
+    if (prs[j].dtype != prs[0].dtype)
+      return set_error(FRN_ERR_INVALID_ARGUMENT, "grouped problems must share one dtype");
+  if (prs[0].dtype != FRN_DTYPE_BF16 && prs[0].dtype != FRN_DTYPE_F16)
+    return set_error(FRN_ERR_UNSUPPORTED, "int8-weight RMSNorm+Linear takes bf16 or fp16 x");
+  // One launch pays off while each problem is one 256-row m-block (per-launch
+  // start and last epilogue dominate: 33.2 -> 25.4 us for Kimi q_b + kv_b at
+  // 256 rows); with more rows the shared tile width costs what the saved
+  // launch gains, so each problem gets its own launch and tile width.
+  if (nprob == 2 && (prs[0].M > 256 || prs[1].M > 256)) {
+    const int rc = run_fused_linear_w8_group(&prs[0], 1, s);
+    return rc ? rc : run_fused_linear_w8_group(&prs[1], 1, s);
+  }
+  if (prs[0].dtype == FRN_DTYPE_BF16) return run_w8_t<__nv_bfloat16>(prs, nprob, s);
+  return run_w8_t<__half>(prs, nprob, s);
+}
+
 int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s) {
-  if (pr.dtype == FRN_DTYPE_BF16) return run_w8_t<__nv_bfloat16>(pr, s);
-  if (pr.dtype == FRN_DTYPE_F16) return run_w8_t<__half>(pr, s);
-  return set_error(FRN_ERR_UNSUPPORTED, "int8-weight RMSNorm+Linear takes bf16 or fp16 x");
+  return run_fused_linear_w8_group(&pr, 1, s);
 }
 
 }  // namespace frn

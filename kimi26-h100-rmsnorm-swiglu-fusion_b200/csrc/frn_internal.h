@@ -108,6 +108,8 @@ int run_fused_linear_decode(const LinearProblem& pr, int split, cudaStream_t s);
 int run_fused_swiglu_decode(const LinearProblem& pr, int64_t inter, int split, cudaStream_t s);
 
 int run_fused_linear_w8(const W8Problem& pr, cudaStream_t s);
+// One or two independent problems of the same dtype in one launch.
+int run_fused_linear_w8_group(const W8Problem* prs, int nprob, cudaStream_t s);
 int run_quantize_int8(int dtype, const void* w, int64_t N, int64_t K, int64_t ws, void* q,
                       int64_t qs, float* scale, cudaStream_t s);
 

@@ -43,6 +43,15 @@ FRN_KERNEL_WIDE_N256 = 14
 FRN_KERNEL_WIDE_N176 = 21
 
 # name -> (restype, argtypes); must cover every function in include/frn_b200.h
+class W8Linear(ctypes.Structure):
+    """struct frn_w8_linear of include/frn_b200.h (one problem of a grouped
+    int8 call)."""
+    _fields_ = [("x", c_void_p), ("M", c_int64), ("K", c_int64), ("x_row_stride", c_int64),
+                ("wq", c_void_p), ("N", c_int64), ("wq_row_stride", c_int64),
+                ("w_scale", c_void_p), ("bias", c_void_p), ("out", c_void_p),
+                ("out_row_stride", c_int64)]
+
+
 PROTOTYPES = {
     "frn_abi_version": (c_int, []),
     "frn_last_error": (c_char_p, []),
@@ -67,6 +76,8 @@ PROTOTYPES = {
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p,
          c_void_p, c_float, c_void_p, c_int64, c_void_p],
     ),
+    "frn_fused_rmsnorm_linear_w8_grouped": (
+        c_int, [c_int, ctypes.POINTER(W8Linear), c_int, c_float, c_void_p]),
     "frn_quantize_int8_per_channel": (
         c_int,
         [c_int, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p],
@@ -213,6 +224,28 @@ def fused_rmsnorm_linear_w8(x, wq, w_scale, bias=None, eps: float = 1e-6, out=No
             out.data_ptr(), out.stride(0), _stream_ptr(x.device))
     check(rc, "frn_fused_rmsnorm_linear_w8")
     return out
+
+
+def fused_rmsnorm_linear_w8_grouped(problems, eps: float = 1e-6):
+    """One launch for one or two independent int8 problems, each a tuple
+    (x, wq, w_scale, bias, out) as in fused_rmsnorm_linear_w8 (out required);
+    returns the outputs."""
+    assert 1 <= len(problems) <= 2
+    arr = (W8Linear * len(problems))()
+    for a, (x, wq, w_scale, bias, out) in zip(arr, problems):
+        assert x.dim() == 2 and wq.dim() == 2 and x.stride(1) == 1 and wq.stride(1) == 1
+        assert x.device == problems[0][0].device and x.dtype == problems[0][0].dtype
+        a.x, a.M, a.K, a.x_row_stride = x.data_ptr(), x.shape[0], x.shape[1], x.stride(0)
+        a.wq, a.N, a.wq_row_stride = wq.data_ptr(), wq.shape[0], wq.stride(0)
+        a.w_scale = w_scale.data_ptr()
+        a.bias = bias.data_ptr() if bias is not None else None
+        a.out, a.out_row_stride = out.data_ptr(), out.stride(0)
+    x0 = problems[0][0]
+    with _on(x0.device):
+        rc = lib().frn_fused_rmsnorm_linear_w8_grouped(_dtype_code(x0), arr, len(problems),
+                                                       float(eps), _stream_ptr(x0.device))
+    check(rc, "frn_fused_rmsnorm_linear_w8_grouped")
+    return [p[4] for p in problems]
 
 
 def quantize_int8_per_channel(w):

@@ -174,13 +174,29 @@ def fused_stack_token_parallel(xs_local: Sequence[torch.Tensor],
     this rank's rows of layer i's input (every rank holds the same rows of
     every layer: its token shard).  Every layer's weights are replicated on
     every rank, so no collective runs; the launches go back to back on the
-    current stream.  Returns the per-layer outputs."""
+    current stream.  Every layer's input is given up front, so no layer
+    feeds another: with the default op, consecutive int8 layers go two per
+    launch (one grouped kernel, e.g. a layer's q_b with its kv_b).  Returns
+    the per-layer outputs."""
     if len(xs_local) != len(layers):
         raise ValueError(f"{len(xs_local)} inputs for {len(layers)} layers")
     outs = []
-    for x, (w, b) in zip(xs_local, layers):
+    i = 0
+    while i < len(layers):
+        x, (w, b) = xs_local[i], layers[i]
+        if (op is None and isinstance(w, tuple) and i + 1 < len(layers)
+                and isinstance(layers[i + 1][0], tuple) and x.is_cuda
+                and xs_local[i + 1].device == x.device and xs_local[i + 1].dtype == x.dtype):
+            from src.load_cuda import denominator_cuda
+
+            x1, (w1, b1) = xs_local[i + 1], layers[i + 1]
+            outs.extend(denominator_cuda.fused_rmsnorm_linear_w8_grouped(
+                x, w[0], w[1], b, x1, w1[0], w1[1], b1, float(eps)))
+            i += 2
+            continue
         f = op or (_default_w8_op() if isinstance(w, tuple) else _default_op())
         outs.append(f(x, w, b, eps))
+        i += 1
     return outs
 
 

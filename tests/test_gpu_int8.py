@@ -90,3 +90,66 @@ def test_int8_rejects_bad_alignment():
     s = torch.ones(8, device=DEV)
     with pytest.raises(capi.FrnError):
         capi.fused_rmsnorm_linear_w8(x, q, s, None, 1e-5)
+
+
+@pytest.mark.parametrize("pair", [
+    ((256, 1536, 12288), (256, 512, 16384)),   # one 8-GPU shard of the int8 stack's layer
+    ((200, 1536, 1000), (129, 64, 264)),        # ragged, different M, N and K, one launch
+    ((256, 512, 16384), (1, 256, 128)),
+    ((1024, 1536, 12288), (1024, 512, 16384)),  # more than one m-block: two launches
+    ((300, 1536, 1000), (129, 64, 264)),
+])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_grouped_int8_matches_separate_calls(pair, dtype):
+    """Two independent problems through the grouped entry point (one launch
+    while both have <= 256 rows): each output against the oracle and
+    bit-identical to its own single-problem launch (same per-element k-order
+    and epilogue, whatever the tile width)."""
+    probs, cases = [], []
+    for i, (M, K, N) in enumerate(pair):
+        x, q, s, b = _case(M, K, N, seed=M + K + N + i, bias=(i == 1), dtype=dtype)
+        cases.append((x, q, s, b))
+        out = torch.empty(M, N, dtype=dtype, device=DEV)
+        probs.append((x.to(DEV), q.to(DEV), s.to(DEV), b.to(DEV) if b is not None else None, out))
+    outs = capi.fused_rmsnorm_linear_w8_grouped(probs, orc.EPS)
+    singles = [capi.fused_rmsnorm_linear_w8(p[0], p[1], p[2], p[3], orc.EPS) for p in probs]
+    torch.cuda.synchronize()
+    for (x, q, s, b), o, o1, shape in zip(cases, outs, singles, pair):
+        _check(o, x, q, s, b, f"grouped {shape}")
+        assert torch.equal(o.view(torch.int16), o1.view(torch.int16)), f"grouped {shape}"
+
+
+def test_grouped_int8_edge_cases():
+    """One problem with no rows runs the other alone; more than two problems
+    and mixed x dtypes are rejected."""
+    x, q, s, b = _case(256, 512, 16384, seed=5)
+    xd, qd, sd = x.to(DEV), q.to(DEV), s.to(DEV)
+    out = torch.empty(256, 16384, dtype=torch.bfloat16, device=DEV)
+    empty = torch.empty(0, 512, dtype=torch.bfloat16, device=DEV)
+    eout = torch.empty(0, 16384, dtype=torch.bfloat16, device=DEV)
+    capi.fused_rmsnorm_linear_w8_grouped([(empty, qd, sd, None, eout), (xd, qd, sd, None, out)],
+                                         orc.EPS)
+    torch.cuda.synchronize()
+    _check(out, x, q, s, None, "grouped with an empty problem")
+    arr = (capi.W8Linear * 3)()
+    rc = capi.lib().frn_fused_rmsnorm_linear_w8_grouped(capi.FRN_DTYPE_BF16, arr, 3, 1e-6, None)
+    assert rc == capi.FRN_ERR_INVALID_ARGUMENT
+
+
+def test_int8_stack_groups_layer_pairs():
+    """fused_stack_token_parallel with int8 layers: consecutive layers share a
+    launch; every output equals its own single-layer call."""
+    from src import multigpu
+    from src.load_cuda import denominator_cuda
+
+    shapes = [(200, 1536, 12288), (200, 512, 16384), (200, 1536, 12288)]  # odd count: last alone
+    xs, layers = [], []
+    for i, (M, K, N) in enumerate(shapes):
+        x, q, s, _ = _case(M, K, N, seed=40 + i)
+        xs.append(x.to(DEV))
+        layers.append(((q.to(DEV), s.to(DEV)), None))
+    outs = multigpu.fused_stack_token_parallel(xs, layers, orc.EPS)
+    for x, ((q, s), _), o in zip(xs, layers, outs):
+        ref = denominator_cuda.fused_rmsnorm_linear_w8(x, q, s, None, orc.EPS)
+        torch.cuda.synchronize()
+        assert torch.equal(o.view(torch.int16), ref.view(torch.int16))
