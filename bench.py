@@ -66,6 +66,7 @@ NVML_REASONS = {
 # Cases --profile can run (one kernel, a few launches, no timing): the linear
 # shapes above plus the int8, SwiGLU and GQA workloads of the sweep.
 PROFILE_CASES = sorted(list(SHAPES) + ["int8_q_b", "int8_q_b_256", "int8_kv_b_256",
+                                       "int8_layer_256",
                                        "swiglu_prefill", "swiglu_decode_m8",
                                        "gqa_decode_llama"])
 # Token-partitioned configurations: (total tokens, hidden, out).
@@ -895,6 +896,21 @@ def run_profile(args):
         for i in range(n):
             j = i % rot.S
             denominator_cuda.fused_rmsnorm_linear(rot.xs[j], rot.wf[j], None, EPS, rot.outs[j])
+    elif case == "int8_layer_256":
+        # one 8-GPU shard of the int8 stack's layer: q_b and kv_b at 256 rows,
+        # one grouped launch
+        sets = []
+        for s in range(4):
+            row = []
+            for K, N in ((1536, 12288), (512, 16384)):
+                x, gamma, W = gpu_inputs(256, K, N, 600 + 2 * s + len(row), device)
+                q, sc = denominator_cuda.quantize_int8_per_channel(W * gamma)
+                row.append((x, q, sc, torch.empty(256, N, dtype=torch.bfloat16, device=device)))
+            sets.append(row)
+        for i in range(n):
+            (xa, qa, sa, oa), (xb, qb, sb, ob) = sets[i % 4]
+            denominator_cuda.fused_rmsnorm_linear_w8_grouped(xa, qa, sa, None, xb, qb, sb, None,
+                                                             EPS, oa, ob)
     elif case.startswith("int8_"):
         M, K, N = {"int8_q_b": (2048, 1536, 12288), "int8_q_b_256": (256, 1536, 12288),
                    "int8_kv_b_256": (256, 512, 16384)}[case]
