@@ -15,7 +15,7 @@
 //
 // CTA (KV head, batch, split), 192 threads: warps 4 and 5 load 64-token K
 // and V stages with TMA (a 3-D view (d, KV head, token) of the cache, 64-d
-// boxes with the 128-byte swizzle) into a 3-slot ring; warps 0-3 each take 16
+// boxes with the 128-byte swizzle) into a 4-slot ring; warps 0-3 each take 16
 // tokens of every stage: ldmatrix (K as the B operand of S, V transposed as
 // the B operand of O), MMAs, online softmax in base 2.  Tokens past the
 // split's end read as -inf scores.  The four warps merge in shared memory;
@@ -47,7 +47,7 @@ struct GqaMmaParams {
 };
 
 constexpr int kGqaStageTokens = 64;
-constexpr int kGqaRing = 3;
+constexpr int kGqaRing = 4;
 
 template <int D>
 struct GqaMmaCfg {
@@ -58,7 +58,7 @@ struct GqaMmaCfg {
   // Cluster-merge receive buffer, a space of its own (peers may write it
   // while this CTA still streams): acc [S][ceil(G*D/S)] (<= 8*D + 7 floats)
   // then max and sum [S][16].
-  static constexpr int OFF_RECV = OFF_BAR + 64;
+  static constexpr int OFF_RECV = OFF_BAR + 128;
   static constexpr int RECV_ACC_FLOATS = 8 * D + 8;
   static constexpr int RECV_FLOATS = RECV_ACC_FLOATS + 8 * 16;
   static constexpr int SMEM_BYTES = OFF_RECV + RECV_FLOATS * 4 + 1024;
@@ -66,7 +66,7 @@ struct GqaMmaCfg {
   // The warp merge reuses the ring: [4 warps][8 heads][D] acc + m + l.
   static constexpr int MERGE_FLOATS = 4 * 8 * D + 2 * 4 * 8;
   static_assert(MERGE_FLOATS * 4 <= OFF_BAR, "merge buffers fit in the ring");
-  static_assert(2 * kGqaRing * 8 + 4 <= 64, "barriers and flag fit before the receive buffer");
+  static_assert(2 * kGqaRing * 8 + 4 <= 128, "barriers and flag fit before the receive buffer");
 };
 
 template <typename T>
