@@ -194,6 +194,10 @@ def _gather_after_peer_left(rank, port, q):
         q.put("gathered")
     except Exception as e:
         q.put(type(e).__name__)
+    # os._exit skips the queue's feeder thread: flush it first, or the
+    # message can be lost.
+    q.close()
+    q.join_thread()
     os._exit(0)
 
 
