@@ -113,14 +113,6 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* m, int32_t c0, int32_t c1,
-                                                int32_t c2) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(m)),
-               "r"(c0), "r"(c1), "r"(c2)
-               : "memory");
-}
-
 // Warms L2 with a 2-D tile (no shared memory written, nothing to wait for).
 // Safe before griddepcontrol.wait: L2 is the coherence point, so a line
 // fetched before the preceding grid writes it is simply updated by that write.
@@ -250,13 +242,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t ra
   return r;
 }
 
-// Arrive on an mbarrier of any CTA in the cluster (release at cluster scope:
-// orders every prior memory access of this thread, global stores included).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-
 // Relaxed remote arrive: no memory ordering beyond the barrier itself.  Used
 // where the only thing to order is tcgen05 work, which the caller fences with
 // tcgen05.fence::before_thread_sync; avoids waiting for outstanding stores.
@@ -360,17 +345,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorM
       : "memory");
 }
 
-// 3-D variant of tma_load_2d_pair.
-__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorMap* m,
-                                                 uint32_t bar_cluster_addr, int32_t c0,
-                                                 int32_t c1, int32_t c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_addr(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_addr(smem_result)),
@@ -398,52 +372,6 @@ __device__ __forceinline__ void umma_f16_ss_pair(uint32_t d_tmem, uint64_t a_des
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
-}
-
-// As umma_f16_ss_pair with A read from tensor memory: each CTA holds its 128
-// rows of A in its own TMEM at a_tmem (row r in lane r, K elements packed two
-// per 32-bit column, so one 16-deep instruction reads 8 columns).  N must be
-// a multiple of 32.
-__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem,
-                                                 uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Asynchronous shared -> tensor memory copy of a 128-row x 32-byte slab (one
-// 16-deep K slice of a K-major bf16/fp16 operand, described like an MMA
-// operand) into lanes 0-127, 8 columns, of both CTAs of the pair: row r lands
-// in lane r, exactly the layout umma_f16_ts_pair reads A in.  Issued by one
-// thread of the even CTA; ordered before later tcgen05.mma of the same thread
-// and tracked by tcgen05.commit.
-__device__ __forceinline__ void tmem_cp_pair_128x256b(uint32_t taddr, uint64_t s_desc) {
-  asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(taddr), "l"(s_desc)
-               : "memory");
-}
-
-// 32 lanes x 32 consecutive 32-bit columns from registers: thread t of the
-// warp writes lane (warp_quarter*32 + t), columns [col, col+32).
-__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
-      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
-      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
-      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
-      "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st_wait() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // Arrive once on the mbarrier at this offset in every CTA of `cta_mask` when
@@ -480,12 +408,6 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ float2 ld_shared_v2f(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
-  return v;
-}
-
 __device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr));
@@ -507,13 +429,6 @@ __device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
-}
-
-__device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
-                                             uint32_t d) {
-  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
-               "r"(d)
-               : "memory");
 }
 
 // ---------------------------------------------------------------- descriptors
