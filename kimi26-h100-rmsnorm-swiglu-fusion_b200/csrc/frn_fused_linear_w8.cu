@@ -105,6 +105,9 @@ struct W8Cfg {
                        WARP_CONV0 = 11, WARP_XLOAD1 = 15;
   static constexpr int THREADS = 32 * 16;
   static_assert(B_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "stage buffers must stay aligned");
+  // The converter warps take the k-block sequence in turn; their parity waits
+  // stay unambiguous only with rings at least as deep as the warps are many.
+  static_assert(STAGES >= CONV_WARPS && QST >= CONV_WARPS, "rings shallower than the converters");
   static_assert(OFF_STG % 1024 == 0, "staging blocks must be 1024-aligned for the 128B swizzle");
   static_assert(SMEM_BYTES <= 232448, "exceeds 227 KB of dynamic shared memory");
 };
@@ -354,6 +357,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
     for (uint32_t i = cw; i < total; i += C::CONV_WARPS) {
       const uint32_t qs = i % QST, qph = (i / QST) & 1u;
       const uint32_t stage = i % STAGES, phase = (i / STAGES) & 1u;
+      // The slot's previous tile (use i - QST, another warp's) has been
+      // released first: only then is qfull[qs] in this use's phase.  A wait on
+      // the parity alone could match that previous phase while it is still
+      // pending (its tile landing after the ones this warp just converted)
+      // and convert a tile that has not arrived.  (The release wait itself
+      // cannot alias: the loader had to see use i - 2*QST released before it
+      // issued use i - 4, which this warp converted, and QST >= 4.)
+      if (!mbar_wait(&qempty[qs], qph ^ 1u, abort_flag, to)) break;
       // The int8 tile has landed, and the main slot's previous MMA is done
       // (its RMS warps released it).
       if (!mbar_wait(&qfull[qs], qph, abort_flag, to)) break;
