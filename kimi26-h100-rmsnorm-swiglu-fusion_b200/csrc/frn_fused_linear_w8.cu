@@ -308,37 +308,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
       bool ok = true;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-       const int nkb = grp.p[j].num_k_blocks;
-       for (int t = tb[j]; t < te[j] && ok; ++t, ++i) {
-        const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
-        if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
-          // As for the pair's TMA loads (data in the odd CTA, complete_tx on this
-          // barrier), a CTA-scope wait suffices: the odd CTA's half arrives as
-          // an st.async complete_tx, itself ordered after that CTA's
-          // fence.proxy.async.  (A cluster-scope acquire here cost ~0.25 us
-          // per k-block on the critical path.)
-          if (!mbar_wait(&conv[stage], phase, abort_flag, to)) { ok = false; break; }
+        const int nkb = grp.p[j].num_k_blocks;
+        for (int t = tb[j]; t < te[j] && ok; ++t, ++i) {
+          const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+          if (!mbar_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, to)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          const uint32_t a_addr = smem_addr(smem + C::OFF_A + stage * C::A_BYTES);
-          const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * C::B_BYTES);
+          const uint32_t d_tmem = tmem_base + acc * BN;
+          for (int kb = 0; kb < nkb; ++kb) {
+            if (!mbar_wait(&full[stage], phase, abort_flag, to)) { ok = false; break; }
+            // As for the pair's TMA loads (data in the odd CTA, complete_tx on this
+            // barrier), a CTA-scope wait suffices: the odd CTA's half arrives as
+            // an st.async complete_tx, itself ordered after that CTA's
+            // fence.proxy.async.  (A cluster-scope acquire here cost ~0.25 us
+            // per k-block on the critical path.)
+            if (!mbar_wait(&conv[stage], phase, abort_flag, to)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_addr = smem_addr(smem + C::OFF_A + stage * C::A_BYTES);
+            const uint32_t b_addr = smem_addr(smem + C::OFF_B + stage * C::B_BYTES);
 #pragma unroll
-          for (int k = 0; k < C::BK / 16; ++k)
-            umma_f16_ss_pair(d_tmem, make_smem_desc_k_sw128(a_addr + k * 32),
-                             make_smem_desc_k_sw128(b_addr + k * 32), idesc,
-                             (kb > 0 || k > 0) ? 1u : 0u);
-          umma_commit_pair_mc(&mma_done[stage], 0x3);
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+            for (int k = 0; k < C::BK / 16; ++k)
+              umma_f16_ss_pair(d_tmem, make_smem_desc_k_sw128(a_addr + k * 32),
+                               make_smem_desc_k_sw128(b_addr + k * 32), idesc,
+                               (kb > 0 || k > 0) ? 1u : 0u);
+            umma_commit_pair_mc(&mma_done[stage], 0x3);
+            if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          umma_commit_pair_mc(&tmem_full[acc], 0x3);
         }
-        if (!ok) break;
-        umma_commit_pair_mc(&tmem_full[acc], 0x3);
-       }
       }
       umma_commit_pair_mc(drain, 0x1);
       uint32_t zero = 0;
@@ -411,43 +411,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
     bool ok = true;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-     const W8Params& pj = grp.p[j];
-     int cur_m = -1;
-     for (int t = tb[j]; t < te[j] && ok; ++t) {
-      const int mb = t / pj.num_n_blocks;
-      const bool first = (mb != cur_m);
-      if (first) { ++gen; cur_m = mb; }
-      float ss0 = 0.f, ss1 = 0.f;
-      for (int kb = 0; kb < pj.num_k_blocks; ++kb) {
-        if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
-        if (first) {
-          const uint32_t row = smem_addr(smem + C::OFF_A + stage * C::A_BYTES) + r * 128;
+      const W8Params& pj = grp.p[j];
+      int cur_m = -1;
+      for (int t = tb[j]; t < te[j] && ok; ++t) {
+        const int mb = t / pj.num_n_blocks;
+        const bool first = (mb != cur_m);
+        if (first) { ++gen; cur_m = mb; }
+        float ss0 = 0.f, ss1 = 0.f;
+        for (int kb = 0; kb < pj.num_k_blocks; ++kb) {
+          if (!mbar_wait(&mma_done[stage], phase, abort_flag, to)) { ok = false; break; }
+          if (first) {
+            const uint32_t row = smem_addr(smem + C::OFF_A + stage * C::A_BYTES) + r * 128;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint4 v = ld_shared_v4(row + ((q ^ (r & 7)) << 4));
-            const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
-            const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
-            ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
-            ss0 = fmaf(f1.x, f1.x, ss0); ss1 = fmaf(f1.y, f1.y, ss1);
-            ss0 = fmaf(f2.x, f2.x, ss0); ss1 = fmaf(f2.y, f2.y, ss1);
-            ss0 = fmaf(f3.x, f3.x, ss0); ss1 = fmaf(f3.y, f3.y, ss1);
+            for (int q = 0; q < 8; ++q) {
+              const uint4 v = ld_shared_v4(row + ((q ^ (r & 7)) << 4));
+              const float2 f0 = pair_to_float2<T>(v.x), f1 = pair_to_float2<T>(v.y);
+              const float2 f2 = pair_to_float2<T>(v.z), f3 = pair_to_float2<T>(v.w);
+              ss0 = fmaf(f0.x, f0.x, ss0); ss1 = fmaf(f0.y, f0.y, ss1);
+              ss0 = fmaf(f1.x, f1.x, ss0); ss1 = fmaf(f1.y, f1.y, ss1);
+              ss0 = fmaf(f2.x, f2.x, ss0); ss1 = fmaf(f2.y, f2.y, ss1);
+              ss0 = fmaf(f3.x, f3.x, ss0); ss1 = fmaf(f3.y, f3.y, ss1);
+            }
           }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
+        if (!ok || !first) continue;
+        const uint32_t g = static_cast<uint32_t>(gen);
+        if (!mbar_wait(&rms_empty[g & 1], ((g >> 1) & 1) ^ 1u, abort_flag, to)) {
+          ok = false;
+          break;
+        }
+        const float inv_k = 1.0f / static_cast<float>(pj.K);
+        rms_buf[(g & 1) * C::BM + r] = rsqrtf((ss0 + ss1) * inv_k + pj.eps);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        if (lane == 0) mbar_arrive(&rms_full[g & 1]);
       }
-      if (!ok || !first) continue;
-      const uint32_t g = static_cast<uint32_t>(gen);
-      if (!mbar_wait(&rms_empty[g & 1], ((g >> 1) & 1) ^ 1u, abort_flag, to)) {
-        ok = false;
-        break;
-      }
-      const float inv_k = 1.0f / static_cast<float>(pj.K);
-      rms_buf[(g & 1) * C::BM + r] = rsqrtf((ss0 + ss1) * inv_k + pj.eps);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rms_full[g & 1]);
-     }
     }
   } else {
     // Epilogue warps 0-3 (as in the bf16 pair kernel, plus scale[n]).
@@ -462,88 +462,89 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W8Cfg<BN, STAGES, QS
     bool ok = true;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-     const W8Params& pj = grp.p[j];
-     int cur_m = -1;
-     for (int t = tb[j]; t < te[j] && ok; ++t, ++i) {
-      const bool has_bias = pj.bias != nullptr;
-      const T* bias = static_cast<const T*>(pj.bias);
-      const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
-      const int mb = t / pj.num_n_blocks;
-      const int row_base = mb * 2 * C::BM + rank * C::BM + q * 32;
-      const int n0 = (t % pj.num_n_blocks) * BN;
-      const bool first = (mb != cur_m);
-      const bool last = (t + 1 >= te[j]) || ((t + 1) / pj.num_n_blocks != mb);
-      const bool reuse_acc = i + 2 < pair_tiles;  // a later tile (of either problem) uses acc
-      if (first) { ++gen; cur_m = mb; }
-      const uint32_t g = static_cast<uint32_t>(gen);
-      // The tile's column scales (0 past N) into this warp's slice; N % 8 == 0,
-      // so a group of 4 columns is either wholly inside or wholly past N.
-      for (int c4 = static_cast<int>(lane); c4 < BN / 4; c4 += 32) {
-        const int col = n0 + c4 * 4;
-        uint4 sv = make_uint4(0u, 0u, 0u, 0u);
-        if (col < pj.N) sv = ld_global_nc_v4(pj.scale + col);
-        st_shared_v4(scl + c4 * 16, sv.x, sv.y, sv.z, sv.w);
-      }
-      __syncwarp();
-      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) {
-        ok = false;
-        break;
-      }
-      if (first) {
-        if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) {
+      const W8Params& pj = grp.p[j];
+      int cur_m = -1;
+      for (int t = tb[j]; t < te[j] && ok; ++t, ++i) {
+        const bool has_bias = pj.bias != nullptr;
+        const T* bias = static_cast<const T*>(pj.bias);
+        const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+        const int mb = t / pj.num_n_blocks;
+        const int row_base = mb * 2 * C::BM + rank * C::BM + q * 32;
+        const int n0 = (t % pj.num_n_blocks) * BN;
+        const bool first = (mb != cur_m);
+        const bool last = (t + 1 >= te[j]) || ((t + 1) / pj.num_n_blocks != mb);
+        const bool reuse_acc = i + 2 < pair_tiles;  // a later tile (of either problem) uses acc
+        if (first) { ++gen; cur_m = mb; }
+        const uint32_t g = static_cast<uint32_t>(gen);
+        // The tile's column scales (0 past N) into this warp's slice; N % 8 == 0,
+        // so a group of 4 columns is either wholly inside or wholly past N.
+        for (int c4 = static_cast<int>(lane); c4 < BN / 4; c4 += 32) {
+          const int col = n0 + c4 * 4;
+          uint4 sv = make_uint4(0u, 0u, 0u, 0u);
+          if (col < pj.N) sv = ld_global_nc_v4(pj.scale + col);
+          st_shared_v4(scl + c4 * 16, sv.x, sv.y, sv.z, sv.w);
+        }
+        __syncwarp();
+        if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, to)) {
           ok = false;
           break;
         }
-        inv_rms = rms_buf[(g & 1) * C::BM + q * 32 + lane];
-      }
-      tc_fence_after();
-      if (last) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
-      }
-      const uint32_t taddr = tmem_base + acc * BN + ((q * 32u) << 16);
-#pragma unroll 1
-      for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
-        const bool half = C::HALF_TAIL && c == C::NCHUNK - 1;
-        const int col0 = n0 + c * 64;
-        uint4 bv[8];
-        if (has_bias) {
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8)
-            bv[c8] = (col0 + c8 * 8 < pj.N && !(half && c8 >= 4))
-                         ? ld_global_nc_v4(bias + col0 + c8 * 8)
-                         : make_uint4(0u, 0u, 0u, 0u);
+        if (first) {
+          if (!mbar_wait(&rms_full[g & 1], (g >> 1) & 1, abort_flag, to)) {
+            ok = false;
+            break;
+          }
+          inv_rms = rms_buf[(g & 1) * C::BM + q * 32 + lane];
         }
-        uint32_t v[64];
-        tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        if (!half) tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-        tmem_ld_wait();
-        if (c == C::NCHUNK - 1 && reuse_acc) {
-          // Only a later tile of this pair waits for this accumulator.
-          tc_fence_before();
+        tc_fence_after();
+        if (last) {
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
+          if (lane == 0) mbar_arrive(&rms_empty[g & 1]);
         }
-        uint8_t* sbp = smem + C::OFF_STG + (q * 2 + (nst & 1u)) * C::STG_BYTES;
-        const uint32_t sb = smem_addr(sbp);
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t cs = scl + c * 64 * 4;
-        if (half) {
-          if (has_bias) stage_rows_swizzled<T, 4, true, true>(v, inv_rms, bv, sb, lane, cs);
-          else stage_rows_swizzled<T, 4, false, true>(v, inv_rms, bv, sb, lane, cs);
-        } else {
-          if (has_bias) stage_rows_swizzled<T, 8, true, true>(v, inv_rms, bv, sb, lane, cs);
-          else stage_rows_swizzled<T, 8, false, true>(v, inv_rms, bv, sb, lane, cs);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(half ? &maps.out_half[j] : &maps.out[j], sbp, col0, row_base);
-          bulk_commit_group();
+        const uint32_t taddr = tmem_base + acc * BN + ((q * 32u) << 16);
+#pragma unroll 1
+        for (int c = 0; c < C::NCHUNK; ++c, ++nst) {
+          const bool half = C::HALF_TAIL && c == C::NCHUNK - 1;
+          const int col0 = n0 + c * 64;
+          uint4 bv[8];
+          if (has_bias) {
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8)
+              bv[c8] = (col0 + c8 * 8 < pj.N && !(half && c8 >= 4))
+                           ? ld_global_nc_v4(bias + col0 + c8 * 8)
+                           : make_uint4(0u, 0u, 0u, 0u);
+          }
+          uint32_t v[64];
+          tmem_ld_32x32b_x32(taddr + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+          if (!half)
+            tmem_ld_32x32b_x32(taddr + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+          tmem_ld_wait();
+          if (c == C::NCHUNK - 1 && reuse_acc) {
+            // Only a later tile of this pair waits for this accumulator.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster_relaxed(leader_tmem_empty0 + acc * 8);
+          }
+          uint8_t* sbp = smem + C::OFF_STG + (q * 2 + (nst & 1u)) * C::STG_BYTES;
+          const uint32_t sb = smem_addr(sbp);
+          if (lane == 0) bulk_wait_group_read<1>();
+          __syncwarp();
+          const uint32_t cs = scl + c * 64 * 4;
+          if (half) {
+            if (has_bias) stage_rows_swizzled<T, 4, true, true>(v, inv_rms, bv, sb, lane, cs);
+            else stage_rows_swizzled<T, 4, false, true>(v, inv_rms, bv, sb, lane, cs);
+          } else {
+            if (has_bias) stage_rows_swizzled<T, 8, true, true>(v, inv_rms, bv, sb, lane, cs);
+            else stage_rows_swizzled<T, 8, false, true>(v, inv_rms, bv, sb, lane, cs);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(half ? &maps.out_half[j] : &maps.out[j], sbp, col0, row_base);
+            bulk_commit_group();
+          }
         }
       }
-     }
     }
     if (lane == 0) bulk_wait_group_read<0>();
   }
